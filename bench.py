@@ -1,0 +1,415 @@
+"""Benchmark of the B200 quantized-linear hot path (vvllm Backend::linear_q8).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (M = 1 decode): the Qwen2.5-7B-shaped int8
+projections -- fused gate/up 3584 -> 37888, down 18944 -> 3584 and lm_head
+3584 -> 152064 -- with fp16 activations, fp32 accumulation and fp16 outputs.
+Weights are synthetic N(0, 0.02), quantized per row by absmax on the GPU;
+activations N(0, 1).  With N GPUs every projection is column-sharded by output
+channel (rank r owns rows [r*N/G, (r+1)*N/G)) and the outputs are all-gathered
+with NCCL, so the total work is fixed as N grows ("strong" scaling).
+
+One step = the three projections once.  `value` is the whole-job algorithmic
+HBM bytes moved per second (int8 weights + fp32 scales + activations in +
+outputs out, summed over ranks), timed on the device with CUDA events over K
+steps, max over ranks.  Weight sets rotate so one cycle per rank exceeds 2x
+the 126 MB L2 (inputs larger than L2).  Output: one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, INTER, VOCAB = 3584, 18944, 152064
+PROJ = [  # name, N (output channels), K (input features)
+    ("gate_up", 2 * INTER, HIDDEN),
+    ("down", HIDDEN, INTER),
+    ("lm_head", VOCAB, HIDDEN),
+]
+METRIC = "linear_q8 GEMV HBM GB/s (% peak) + prefill GEMM TFLOP/s at Qwen-0.5B/7B shapes"
+WORKLOAD = "qwen2.5-7b-shaped decode projections (gate_up 3584->37888, down 18944->3584, lm_head 3584->152064), M=1"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def algo_bytes(N: int, K: int, M: int = 1, a: int = 2, o: int = 2) -> int:
+    """int8 weights + fp32 scales + activations in + outputs out (weights read once)."""
+    return N * K + 4 * N + M * K * a + M * N * o
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons = [], 0
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - no NVML here
+            self.err = str(e)
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def cpu_info():
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return name, os.cpu_count() or 1
+
+
+def cpu_reference_lib():
+    """The reference's own CPU linear_q8 (oracle/_ref) if it was built, else the C restatement."""
+    from oracle import Oracle, Reference, have_reference
+
+    if have_reference():
+        return Reference(), "reference"
+    return Oracle(), "port"
+
+
+def time_cpu_linear(lib, shapes, threads: int, budget_s: float, min_iters: int = 1):
+    """Times lib.linear_q8_mt over `shapes` (list of (x, q, s)); returns (GB/s, seconds/iter, iters)."""
+    total_bytes = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
+    for x, q, s in shapes:  # warm the pages
+        lib.linear_q8_mt(x, q, s, None, nthreads=threads)
+    iters, t0 = 0, time.perf_counter()
+    while True:
+        for x, q, s in shapes:
+            lib.linear_q8_mt(x, q, s, None, nthreads=threads)
+        iters += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s and iters >= min_iters:
+            break
+    return total_bytes * iters / el / 1e9, el / iters, iters
+
+
+def host_sample_weights(frac_rows: float, seed: int = 0):
+    """Host int8 weights for a row sample of every projection (values do not change CPU timing)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, N, K in PROJ:
+        n = max(1, int(N * frac_rows))
+        q = rng.integers(-127, 128, size=(n, K), dtype=np.int8)
+        s = (rng.random(n, dtype=np.float32) * np.float32(1e-3)).astype(np.float32)
+        x = rng.standard_normal((1, K), dtype=np.float32).astype(np.float16).astype(np.float32)
+        out.append((x, q, s))
+    return out
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU linear_q8 on all host threads, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    lib, kind = cpu_reference_lib()
+    model, cores = cpu_info()
+    frac = args.cpu_sample
+    shapes = host_sample_weights(frac)
+    sample_bytes = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
+    for _ in range(args.warmup):
+        for x, q, s in shapes:
+            lib.linear_q8_mt(x, q, s, None, nthreads=cores)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for x, q, s in shapes:
+            lib.linear_q8_mt(x, q, s, None, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    el = sum(times)
+    gbs = sample_bytes * args.steps / el / 1e9
+    sample = (f"{frac:.3f} of the rows of each projection ({sample_bytes / 1e6:.1f} MB algorithmic per step), "
+              f"fp32 activations widened from fp16, {cores} threads on disjoint output-channel slices; "
+              f"CPU: {model}")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * el / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 weights x f32 activations, f32 accumulate",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-sample", type=float, default=0.125,
+                    help="fraction of each projection's rows timed on the CPU")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import vvllm_b200 as v
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    hbm_peak, tc_peak, peak_kind = peaks()
+
+    # ---- weights (per rank shard), made and quantized on the device -------------------------
+    gen = torch.Generator(device=dev)
+    shards = []
+    for pi, (name, N, K) in enumerate(PROJ):
+        r0, rows = v.shard_range(N, world, rank)
+        q = torch.empty((rows, K), dtype=torch.int8, device=dev)
+        s = torch.empty((rows,), dtype=torch.float32, device=dev)
+        step = 8192
+        for a in range(0, rows, step):  # quantize in slabs to bound the fp32 staging memory
+            b = min(rows, a + step)
+            gen.manual_seed(1000 + 16 * 28 + pi * 1000003 + r0 + a)
+            w = torch.randn((b - a, K), generator=gen, device=dev) * 0.02
+            v.quantize_per_channel(w, q[a:b], s[a:b])
+        shards.append((name, N, K, r0, rows, q, s))
+    torch.cuda.synchronize()
+    per_rank_bytes = sum(algo_bytes(rows, K) for _, _, K, _, rows, _, _ in shards)
+    copies = max(1, math.ceil(2 * L2_BYTES / per_rank_bytes))
+    sets = [[(q, s) for (_, _, _, _, _, q, s) in shards]]
+    for _ in range(copies - 1):
+        sets.append([(q.clone(), s.clone()) for (_, _, _, _, _, q, s) in shards])
+    xs = [torch.randn((1, K), generator=gen, device=dev).half() for (_, _, K, _, _, _, _) in shards]
+    per = [-(-N // world) for (_, N, _, _, _, _, _) in shards]
+    outs = [torch.empty((1, p * world), dtype=torch.float16, device=dev) for p in per]
+
+    comm = None
+    if world > 1:
+        uid = [v.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = v.Comm(local, world, rank, uid[0], timeout_s=120.0)
+
+    stream = torch.cuda.current_stream()
+    L = v.lib()
+    lm_idx = [n for n, *_ in PROJ].index("lm_head")
+
+    def step(it, ev=None):
+        ws = sets[it % copies]
+        for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
+            q, s = ws[i]
+            slot = outs[i][:, rank * per[i]: rank * per[i] + rows]
+            if ev is not None and i == lm_idx:
+                ev[0].record(stream)
+            v.linear_q8(slot, xs[i], q, s, None, stream=stream)
+            if ev is not None and i == lm_idx:
+                ev[1].record(stream)
+            if comm is not None:
+                comm.allgather(outs[i], per[i], v.F16, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for it in range(args.warmup):
+        step(it)
+    barrier()
+
+    lm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier()
+        n0 = v.launch_count()
+        t_start.record(stream)
+        for it in range(args.steps):
+            step(it, lm_events[it])
+        t_end.record(stream)
+        barrier()
+        n_launch = v.launch_count() - n0
+    ms = t_start.elapsed_time(t_end)
+    lm_ms = statistics.mean(a.elapsed_time(b) for a, b in lm_events)
+    if world > 1:
+        t = torch.tensor([ms, lm_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, lm_ms = t.tolist()
+    ms_step = ms / args.steps
+    total_bytes = sum(algo_bytes(N, K) for _, N, K in PROJ)  # whole job, all ranks
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+    lm_rows = shards[lm_idx][4]
+    lm_bytes = algo_bytes(lm_rows, HIDDEN)
+    lm_gbs = lm_bytes / (lm_ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with host buffers -------------------------------------
+    h_in = [torch.empty((1, K), dtype=torch.float16).pin_memory() for (_, _, K, _, _, _, _) in shards]
+    for h, x in zip(h_in, xs):
+        h.copy_(x.cpu())
+    h_out = [torch.empty((1, N), dtype=torch.float16).pin_memory() for (_, N, _, _, _, _, _) in shards]
+    h2d = sum(h.numel() * 2 for h in h_in)
+    d2h = sum(h.numel() * 2 for h in h_out)
+    d_in = [torch.empty_like(x) for x in xs]
+
+    def e2e_step(it):
+        ws = sets[it % copies]
+        for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
+            d_in[i].copy_(h_in[i], non_blocking=True)
+            q, s = ws[i]
+            if comm is None:
+                v.linear_q8(outs[i][:, :N], d_in[i], q, s, None, stream=stream)
+            else:
+                v.linear_q8_sharded(comm, outs[i][:, :N] if N % world == 0 else outs[i], d_in[i], q, s,
+                                    None, N, gather=None if N % world == 0 else outs[i], stream=stream)
+            h_out[i].copy_(outs[i][:, :N], non_blocking=True)
+
+    for it in range(args.warmup):
+        e2e_step(it)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for it in range(args.steps):
+        e2e_step(it)
+    e1.record(stream)
+    barrier()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = t.item()
+    e2e_value = total_bytes / (e_ms / args.steps * 1e-3) / 1e9
+
+    # ---- CPU baseline: the reference's linear_q8 on the host cores (rank 0, N = 1) ------------
+    cpu_baseline = None
+    if world == 1 and not args.no_cpu_baseline:
+        lib, kind = cpu_reference_lib()
+        model, cores = cpu_info()
+        shapes = host_sample_weights(args.cpu_sample)
+        gbs, sec, iters = time_cpu_linear(lib, shapes, cores, args.cpu_budget)
+        sb = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
+        cpu_baseline = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                        "sample": f"{args.cpu_sample:.3f} of each projection's rows "
+                                  f"({sb / 1e6:.1f} MB algorithmic), {iters} passes in {sec * iters:.1f} s, "
+                                  f"{cores} threads; CPU: {model}"}
+
+    if rank == 0:
+        traffic = profiled_traffic("q8_gemv_lm_head")
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 weights x f16 activations, f32 accumulate", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": 1, "activations": "fp16", "parallelism": f"column-shard x{world}",
+                       "collective": "NCCL allgather" if world > 1 else "none",
+                       "l2": f"{copies} rotating weight set(s), {copies * per_rank_bytes / 1e6:.0f} MB per rank per cycle (> L2)"},
+            "roofline": {"bound": "hbm", "kernel": "q8_gemv (lm_head shard)", "achieved": round(lm_gbs, 2),
+                         "peak": hbm_peak, "unit": "GB/s", "frac": round(lm_gbs / hbm_peak, 4),
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": round(lm_ms, 5)},
+            "pct_of_hbm_peak": round(100 * value / (hbm_peak * world), 2),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms / args.steps, 5)},
+            "gpu_launches": int(n_launch),
+            "clocks": sampler.summary(),
+        }
+        if cpu_baseline is not None:
+            line["cpu_baseline"] = cpu_baseline
+        print(json.dumps(line), flush=True)
+
+    if comm is not None:
+        comm.destroy()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,163 @@
+/*
+ * b200q8.h -- C ABI of the B200 (sm_100a) quantized-linear library.
+ *
+ * This is the drop-in boundary for vvllm's quantized linear hot path
+ * (hoobean1996/vvllm).  Every entry point returns an int status (0 = ok,
+ * negative = error, see B200Q8_ERR_*) and never exits the process; the
+ * message for the last failure on the calling thread is b200q8_last_error().
+ * No entry point has a CPU fallback: if the GPU path cannot run, it fails.
+ *
+ * Three layers:
+ *   1. kernel layer  -- device pointers, caller's stream, no allocation;
+ *   2. backend layer -- the exact argument conventions of vvllm::Backend
+ *      (device activations, host weight pointers cached on first use);
+ *   3. sharded layer -- output-channel column sharding over NCCL.
+ *
+ * Types: int8 weights are row-major [N, K] with one fp32 scale per output row
+ * (per-channel absmax).  Activations are fp32 or fp16 ("half", IEEE binary16);
+ * all accumulation is fp32.
+ */
+#ifndef B200Q8_H
+#define B200Q8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B200Q8_API __attribute__((visibility("default")))
+#else
+#define B200Q8_API
+#endif
+
+/* Same object as cudaStream_t (NULL = the legacy default stream). */
+typedef struct CUstream_st* b200q8_stream_t;
+
+#define B200Q8_ABI_VERSION 1
+
+/* Status codes. */
+#define B200Q8_OK 0
+#define B200Q8_ERR_INVALID (-1)     /* bad argument (null pointer, bad dtype, size overflow) */
+#define B200Q8_ERR_CUDA (-2)        /* a CUDA runtime / driver call failed */
+#define B200Q8_ERR_UNSUPPORTED (-3) /* shape or device the kernels do not handle */
+#define B200Q8_ERR_NCCL (-4)        /* an NCCL call failed or NCCL is unavailable */
+#define B200Q8_ERR_TIMEOUT (-5)     /* a bounded wait (NCCL init, peer flag) ran out */
+#define B200Q8_ERR_ALLOC (-6)       /* device allocation failed */
+
+/* Element types of activations / outputs. */
+#define B200Q8_F32 0
+#define B200Q8_F16 1
+
+B200Q8_API int b200q8_abi_version(void);
+/* Message of the last failing call made on this thread ("" if none). */
+B200Q8_API const char* b200q8_last_error(void);
+/* Number of kernel launches this library has issued in this process. */
+B200Q8_API uint64_t b200q8_launch_count(void);
+
+/* ------------------------------------------------------------------------
+ * 1. Kernel layer.  All pointers are device pointers; work is enqueued on
+ *    `stream` and the call returns without synchronising.
+ * ------------------------------------------------------------------------ */
+
+/* q[N,K], scales[N] = per-row absmax int8 quantization of w[N,K] (fp32).
+ * Bit-identical to vvllm::quantize_per_channel
+ * (replaces include/vvllm/quantize/quantize.h:18, src/quantize/quantize.cc:9-48). */
+B200Q8_API int b200q8_quantize_per_channel(const float* w, size_t N, size_t K, int8_t* q, float* scales,
+                                b200q8_stream_t stream);
+
+/* out[M,N] = (inp[M,K] . float(weight[N,K])^T) * scales[N] + bias[N]
+ * bias may be NULL.  inp is fp32 or fp16 (in_dtype); out is fp32 or fp16
+ * (out_dtype).  inp must not overlap out.
+ * Replaces vvllm::Backend::linear_q8 (include/vvllm/backend/backend.h:62-65)
+ * as implemented by BackendCPU (src/backend/backend_naive.cc:155-291) and
+ * BackendCUDA (src/backend/backend_cuda.cc:188-213). */
+B200Q8_API int b200q8_linear_q8(void* out, int out_dtype, const void* inp, int in_dtype,
+                     const int8_t* weight, const float* scales, const float* bias, size_t M,
+                     size_t N, size_t K, b200q8_stream_t stream);
+
+/* As b200q8_linear_q8, plus residual[M,N] (same dtype as out) added last.
+ * out may be the same pointer as residual (in-place residual connection).
+ * Replaces vvllm::Backend::linear_q8_add (include/vvllm/backend/backend.h:75-78;
+ * src/backend/backend_naive.cc:322-335, src/backend/backend_cuda.cc:246-275). */
+B200Q8_API int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype,
+                         const int8_t* weight, const float* scales, const float* bias,
+                         const void* residual, size_t M, size_t N, size_t K,
+                         b200q8_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * 2. Backend layer.  Mirrors vvllm::BackendCUDA's hot-path conventions:
+ *    activations (out, inp, residual) are device pointers, fp32 or -- when the
+ *    backend was created with fp16=1 -- fp16 data behind float* pointers
+ *    (include/vvllm/model/transformer.h:82,93); weight, scales and bias are
+ *    HOST pointers, uploaded on first use and cached by host address for the
+ *    backend's lifetime (src/backend/backend_cuda.cc:51-77).  The int8 weight
+ *    stays int8 on the device: no fp16 copy is ever built.
+ * ------------------------------------------------------------------------ */
+typedef struct b200q8_backend b200q8_backend;
+
+/* Replaces BackendCUDA::BackendCUDA(bool fp16) (src/backend/backend_cuda.cc:13-26). */
+B200Q8_API int b200q8_backend_create(int device, int fp16, b200q8_backend** out);
+B200Q8_API int b200q8_backend_destroy(b200q8_backend* be);
+/* Stream used by the backend calls (default: the legacy default stream). */
+B200Q8_API int b200q8_backend_set_stream(b200q8_backend* be, b200q8_stream_t stream);
+/* Bytes of device memory held by the weight cache. */
+B200Q8_API int b200q8_backend_cached_bytes(const b200q8_backend* be, size_t* bytes);
+
+/* Backend::linear_q8 (include/vvllm/backend/backend.h:64-65). */
+B200Q8_API int b200q8_backend_linear_q8(b200q8_backend* be, float* out, const float* inp,
+                             const int8_t* weight, const float* scales, const float* bias,
+                             size_t M, size_t N, size_t K);
+/* Backend::linear_q8_add (include/vvllm/backend/backend.h:76-78); out may equal residual. */
+B200Q8_API int b200q8_backend_linear_q8_add(b200q8_backend* be, float* out, const float* inp,
+                                 const int8_t* weight, const float* scales, const float* bias,
+                                 const float* residual, size_t M, size_t N, size_t K);
+/* quantize_per_channel with host input and host outputs, run on the GPU
+ * (include/vvllm/quantize/quantize.h:18): q[N*K], scales[N]. */
+B200Q8_API int b200q8_backend_quantize_per_channel(b200q8_backend* be, const float* weight, size_t N,
+                                        size_t K, int8_t* q, float* scales);
+
+/* ------------------------------------------------------------------------
+ * 3. Sharded layer: output-channel (column) sharding of one projection over
+ *    G GPUs of one node, outputs all-gathered over NVLink with NCCL.  The
+ *    reference has no multi-GPU path; there is no counterpart to cite.
+ * ------------------------------------------------------------------------ */
+typedef struct b200q8_comm b200q8_comm;
+
+/* Rows [row0, row0 + rows) of an N-row weight belong to `rank` of `nranks`:
+ * every rank owns ceil(N / nranks) rows except the tail ranks. */
+B200Q8_API int b200q8_shard_range(size_t N, int nranks, int rank, size_t* row0, size_t* rows);
+
+/* 128-byte NCCL unique id, made on one rank and sent to the others by the caller. */
+B200Q8_API int b200q8_comm_unique_id(uint8_t id[128]);
+/* Non-blocking NCCL communicator init, polled until `timeout_s` runs out
+ * (then the communicator is aborted and B200Q8_ERR_TIMEOUT returned). */
+B200Q8_API int b200q8_comm_init(int device, int nranks, int rank, const uint8_t id[128], double timeout_s,
+                     b200q8_comm** out);
+B200Q8_API int b200q8_comm_destroy(b200q8_comm* comm);
+/* Aborts outstanding NCCL work and frees the communicator. */
+B200Q8_API int b200q8_comm_abort(b200q8_comm* comm);
+
+/* In-place all-gather of equal slices: rank r's `count` elements sit at
+ * buf + r * count (elements of `dtype`) and every rank ends with all of them. */
+B200Q8_API int b200q8_comm_allgather(b200q8_comm* comm, void* buf, size_t count, int dtype,
+                                     b200q8_stream_t stream);
+
+/* Each rank computes its shard out_local[M, rows] = linear_q8 over its weight
+ * rows (w_shard [rows, K], scales_shard, bias_shard), then all ranks gather
+ * out[M, N].  out_dtype F16 or F32.  `gather` is caller scratch of
+ * nranks * M * ceil(N/nranks) elements of out_dtype; it may be NULL when
+ * M == 1 and nranks divides N (the gather then lands in `out` directly).
+ * Stream-ordered on `stream`. */
+B200Q8_API int b200q8_linear_q8_sharded(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
+                             int in_dtype, const int8_t* w_shard, const float* scales_shard,
+                             const float* bias_shard, size_t M, size_t N, size_t K, void* gather,
+                             b200q8_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q8_H */

@@ -1,0 +1,223 @@
+"""GPU parity of b200q8_linear_q8 / _add (through the C ABI) against the CPU oracle.
+
+Tolerances (normwise over each token row, max|y - y_ref| / max|y_ref|):
+  fp32 activations: 1e-5      fp16 activations: 2e-3 (after the kernel's fp16 rounding)
+The fp16 oracle runs on the exact fp32 widening of the same fp16 inputs.
+"""
+import os
+import zlib
+
+import numpy as np
+import pytest
+
+from tests._util import (TOL_F16, TOL_F32, make_bias, make_weight, make_x, rowwise_normwise_err,
+                         sample_rows)
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _t(a, dev, dtype=None):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def run_gpu(cuda, x, q, s, b=None, res=None, in16=False, out16=False, inplace=False):
+    """Runs the kernel; returns (y as fp32 numpy, oracle inputs x_eff, res_eff)."""
+    import torch
+
+    import vvllm_b200 as v
+
+    xt = _t(x, cuda, torch.float16 if in16 else torch.float32)
+    qt, st = _t(q, cuda), _t(s, cuda)
+    bt = _t(b, cuda) if b is not None else None
+    odt = torch.float16 if out16 else torch.float32
+    M, N = x.shape[0], q.shape[0]
+    if res is not None:
+        rt = _t(res, cuda, odt)
+        res_eff = rt.float().cpu().numpy()
+        out = rt if inplace else torch.empty((M, N), dtype=odt, device=cuda)
+        v.linear_q8_add(out, xt, qt, st, bt, rt)
+    else:
+        res_eff = None
+        out = torch.empty((M, N), dtype=odt, device=cuda)
+        v.linear_q8(out, xt, qt, st, bt)
+    torch.cuda.synchronize()
+    x_eff = xt.float().cpu().numpy()
+    return out.float().cpu().numpy(), x_eff, res_eff
+
+
+def oracle_ref(oracle, x_eff, q, s, b, res_eff):
+    if res_eff is not None:
+        return oracle.linear_q8_add(x_eff, q, s, b, res_eff)
+    return oracle.linear_q8(x_eff, q, s, b)
+
+
+def test_golden_cases_fp32(cuda):
+    """The reference's own outputs (tests/golden/linear_small.npz) at 1e-5."""
+    g = np.load(os.path.join(GOLD, "linear_small.npz"))
+    idx = 0
+    while f"c{idx}_q" in g:
+        p = f"c{idx}_"
+        b = g[p + "b"] if p + "b" in g else None
+        r = g[p + "r"] if p + "r" in g else None
+        y, _, _ = run_gpu(cuda, g[p + "x"], g[p + "q"], g[p + "s"], b, r, inplace=r is not None)
+        err = rowwise_normwise_err(y, g[p + "y"])
+        assert err <= TOL_F32, (p, err)
+        idx += 1
+
+
+SHAPES = [
+    # name, M, N, K
+    ("config1", 1, 4864, 896),
+    ("smol_q", 1, 576, 576), ("smol_kv", 1, 192, 576), ("smol_up", 1, 1536, 576),
+    ("smol_down", 1, 576, 1536),
+    ("qwen_q", 1, 896, 896), ("qwen_kv", 1, 128, 896), ("qwen_gate_up", 1, 9728, 896),
+    ("qwen_down", 1, 896, 4864),
+    ("q7b_down_shard8", 1, 448, 18944), ("q7b_up_shard8", 1, 4736, 3584),
+    ("m2", 2, 1000, 896), ("m3", 3, 333, 1536), ("m4", 4, 4864, 896), ("m5", 5, 300, 576),
+    ("m8", 8, 512, 896), ("m17", 17, 100, 3584),
+]
+
+
+@pytest.mark.parametrize("in16,out16", [(False, False), (True, True), (True, False), (False, True)])
+@pytest.mark.parametrize("name,M,N,K", SHAPES)
+def test_linear_shapes(cuda, oracle, name, M, N, K, in16, out16):
+    w = make_weight(N, K, zlib.crc32(name.encode()) % 1000 + 1)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 42)
+    b = make_bias(N, 7) if name.startswith("qwen_q") or name.startswith("qwen_kv") or M > 1 else None
+    y, xe, _ = run_gpu(cuda, x, q, s, b, in16=in16, out16=out16)
+    ref = oracle_ref(oracle, xe, q, s, b, None)
+    tol = TOL_F16 if (in16 or out16) else TOL_F32
+    err = rowwise_normwise_err(y, ref)
+    assert err <= tol, err
+
+
+@pytest.mark.parametrize("in16", [False, True])
+@pytest.mark.parametrize("M,N,K", [(1, 896, 896), (1, 896, 4864), (3, 576, 1536), (6, 200, 896)])
+def test_linear_add_inplace_and_separate(cuda, oracle, M, N, K, in16):
+    w = make_weight(N, K, 11)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 12)
+    res = make_x(M, N, 13)
+    tol = TOL_F16 if in16 else TOL_F32
+    for inplace in (True, False):
+        y, xe, re = run_gpu(cuda, x, q, s, None, res, in16=in16, out16=in16, inplace=inplace)
+        ref = oracle_ref(oracle, xe, q, s, None, re)
+        assert rowwise_normwise_err(y, ref) <= tol
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 7, 17), (2, 5, 33), (1, 1, 1), (3, 64, 100), (1, 31, 48)])
+def test_ragged_k_generic_path(cuda, oracle, M, N, K):
+    w = make_weight(N, K, 21)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 22)
+    b = make_bias(N, 23)
+    y, xe, _ = run_gpu(cuda, x, q, s, b)
+    assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, None)) <= TOL_F32
+
+
+def test_misaligned_pointers(cuda, oracle):
+    """Activation/weight views at odd offsets take the generic kernel and stay correct."""
+    import torch
+
+    import vvllm_b200 as v
+
+    N, K = 300, 896
+    w = make_weight(N, K, 31)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(1, K, 32)
+    xb = torch.zeros(K + 3, device=cuda)
+    xb[3:] = torch.from_numpy(x[0]).to(cuda)
+    qb = torch.zeros(N * K + 5, dtype=torch.int8, device=cuda)
+    qb[5:] = torch.from_numpy(q.ravel()).to(cuda)
+    out = torch.empty((1, N), device=cuda)
+    L = v.lib()
+    st = L.b200q8_linear_q8(out.data_ptr(), 0, xb[3:].data_ptr(), 0, qb[5:].data_ptr(),
+                            torch.from_numpy(s).to(cuda).data_ptr(), None, 1, N, K, None)
+    assert st == 0
+    torch.cuda.synchronize()
+    ref = oracle.linear_q8(x, q, s, None)
+    assert rowwise_normwise_err(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_deterministic(cuda, oracle):
+    import torch
+
+    import vvllm_b200 as v
+
+    N, K = 4864, 896
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 41))
+    xt = torch.from_numpy(make_x(1, K, 42)).to(cuda)
+    qt, st = torch.from_numpy(q).to(cuda), torch.from_numpy(s).to(cuda)
+    outs = []
+    for _ in range(3):
+        o = torch.empty((1, N), device=cuda)
+        v.linear_q8(o, xt, qt, st)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+def test_empty_and_streams(cuda, oracle):
+    import torch
+
+    import vvllm_b200 as v
+
+    q, s = oracle.quantize_per_channel(make_weight(64, 64, 51))
+    qt, st = torch.from_numpy(q).to(cuda), torch.from_numpy(s).to(cuda)
+    x = torch.randn(0, 64, device=cuda)
+    out = torch.empty(0, 64, device=cuda)
+    v.linear_q8(out, x, qt, st)  # M = 0: no-op
+    side = torch.cuda.Stream()
+    x1 = torch.from_numpy(make_x(1, 64, 52)).to(cuda)
+    o1 = torch.empty(1, 64, device=cuda)
+    side.wait_stream(torch.cuda.current_stream())
+    v.linear_q8(o1, x1, qt, st, stream=side)
+    side.synchronize()
+    ref = oracle.linear_q8(x1.cpu().numpy(), q, s, None)
+    assert rowwise_normwise_err(o1.cpu().numpy(), ref) <= TOL_F32
+
+
+LARGE = [
+    # name, N, K, M  -- BASELINE config 3 lm_head and config 5 (7B) shapes at full size
+    ("qwen05b_lm_head", 151936, 896, 1),
+    ("q7b_gate_up", 37888, 3584, 1),
+    ("q7b_down", 3584, 18944, 1),
+    ("q7b_lm_head", 152064, 3584, 1),
+    ("q7b_gate_up_m8", 37888, 3584, 8),
+    ("q7b_down_m64", 3584, 18944, 64),
+]
+
+
+@pytest.mark.parametrize("name,N,K,M", LARGE)
+def test_full_size_sampled_rows(cuda, oracle, name, N, K, M):
+    """Full-size weights made and quantized on the GPU; a row sample is checked on the CPU:
+    the GPU quantization of those rows bit-exactly, the fp16 outputs within 2e-3."""
+    import torch
+
+    import vvllm_b200 as v
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(zlib.crc32(name.encode()) % 10000)
+    w = torch.randn((N, K), generator=g, device=cuda, dtype=torch.float32) * 0.02
+    q = torch.empty((N, K), dtype=torch.int8, device=cuda)
+    s = torch.empty((N,), dtype=torch.float32, device=cuda)
+    v.quantize_per_channel(w, q, s)
+    x = torch.randn((M, K), generator=g, device=cuda).half()
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    v.linear_q8(out, x, q, s)
+    torch.cuda.synchronize()
+    rows = torch.from_numpy(sample_rows(N, 384)).to(cuda)
+    w_rows = w[rows].cpu().numpy()
+    q_rows, s_rows = q[rows].cpu().numpy(), s[rows].cpu().numpy()
+    del w
+    oq, os_ = oracle.quantize_per_channel(w_rows)
+    assert np.array_equal(oq, q_rows)
+    assert np.array_equal(os_.view(np.uint32), s_rows.view(np.uint32))
+    ref = oracle.linear_q8(x.float().cpu().numpy(), q_rows, s_rows, None)
+    y = out[:, rows].float().cpu().numpy()
+    assert rowwise_normwise_err(y, ref) <= TOL_F16

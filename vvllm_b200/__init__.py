@@ -1,0 +1,22 @@
+"""vvllm_b200 -- B200 (sm_100a) quantized-linear hot path of vvllm.
+
+The product is ``libb200q8.so`` (CUDA kernels + the C ABI in
+``include/b200q8.h``).  This package only binds that library with ctypes so
+the tests and ``bench.py`` call exactly what a C/C++ caller would; it contains
+no compute of its own and no CPU fallback.  If the library is missing or a
+call fails, an exception is raised.
+"""
+from ._lib import (  # noqa: F401
+    B200Q8Error,
+    F16,
+    F32,
+    Backend,
+    Comm,
+    lib,
+    launch_count,
+    linear_q8,
+    linear_q8_add,
+    linear_q8_sharded,
+    quantize_per_channel,
+    shard_range,
+)

@@ -1,0 +1,230 @@
+"""ctypes binding of libb200q8.so (include/b200q8.h).
+
+Device buffers are passed as raw addresses (``int``) or torch CUDA tensors;
+streams as ``cudaStream_t`` addresses (``torch.cuda.Stream.cuda_stream``).
+Every wrapper checks the returned status and raises ``B200Q8Error`` with the
+library's message.  Nothing here computes: the shared library does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200q8.so")
+
+F32 = 0
+F16 = 1
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_int = ctypes.c_int
+
+
+class B200Q8Error(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"b200q8 status {status}: {msg}")
+        self.status = status
+
+
+_SIGS = {
+    "b200q8_abi_version": ([], _int),
+    "b200q8_last_error": ([], ctypes.c_char_p),
+    "b200q8_launch_count": ([], ctypes.c_uint64),
+    "b200q8_quantize_per_channel": ([_vp, _sz, _sz, _vp, _vp, _vp], _int),
+    "b200q8_linear_q8": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_backend_create": ([_int, _int, ctypes.POINTER(_vp)], _int),
+    "b200q8_backend_destroy": ([_vp], _int),
+    "b200q8_backend_set_stream": ([_vp, _vp], _int),
+    "b200q8_backend_cached_bytes": ([_vp, ctypes.POINTER(_sz)], _int),
+    "b200q8_backend_linear_q8": ([_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz], _int),
+    "b200q8_backend_linear_q8_add": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz], _int),
+    "b200q8_backend_quantize_per_channel": ([_vp, _vp, _sz, _sz, _vp, _vp], _int),
+    "b200q8_shard_range": ([_sz, _int, _int, ctypes.POINTER(_sz), ctypes.POINTER(_sz)], _int),
+    "b200q8_comm_unique_id": ([ctypes.c_char_p], _int),
+    "b200q8_comm_init": ([_int, _int, _int, ctypes.c_char_p, ctypes.c_double, ctypes.POINTER(_vp)], _int),
+    "b200q8_comm_destroy": ([_vp], _int),
+    "b200q8_comm_abort": ([_vp], _int),
+    "b200q8_comm_allgather": ([_vp, _vp, _sz, _int, _vp], _int),
+    "b200q8_linear_q8_sharded": (
+        [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp], _int),
+}
+
+# Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
+EXPORTED = tuple(_SIGS)
+
+_lib = None
+
+
+def lib():
+    """Load libb200q8.so once; raise if it is absent (there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise B200Q8Error(-3, f"{LIB_PATH} not built (run `python -m vvllm_b200.build`)")
+        L = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+        for name, (args, res) in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = lib().b200q8_last_error().decode(errors="replace")
+        raise B200Q8Error(status, msg)
+
+
+def _addr(t) -> int | None:
+    """Device address of a torch tensor / int / None."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(s) -> int | None:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.float16:
+        return F16
+    raise TypeError(f"unsupported activation dtype {t.dtype}")
+
+
+def launch_count() -> int:
+    return int(lib().b200q8_launch_count())
+
+
+def quantize_per_channel(w, q, scales, stream=None) -> None:
+    """q[N,K] int8, scales[N] fp32 = per-row absmax quantization of w[N,K] fp32 (device)."""
+    N, K = w.shape
+    _check(lib().b200q8_quantize_per_channel(_addr(w), N, K, _addr(q), _addr(scales), _stream(stream)))
+
+
+def linear_q8(out, x, w, scales, bias=None, stream=None) -> None:
+    """out[M,N] = (x[M,K] . W^T) * scales + bias, x/out fp32 or fp16 torch CUDA tensors."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib().b200q8_linear_q8(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x), _addr(w),
+                                  _addr(scales), _addr(bias), M, N, K, _stream(stream)))
+
+
+def linear_q8_add(out, x, w, scales, bias, residual, stream=None) -> None:
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib().b200q8_linear_q8_add(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x),
+                                      _addr(w), _addr(scales), _addr(bias), _addr(residual), M, N,
+                                      K, _stream(stream)))
+
+
+def shard_range(N: int, nranks: int, rank: int) -> tuple[int, int]:
+    r0, n = _sz(), _sz()
+    _check(lib().b200q8_shard_range(N, nranks, rank, ctypes.byref(r0), ctypes.byref(n)))
+    return r0.value, n.value
+
+
+class Backend:
+    """vvllm::Backend-shaped handle: host weight pointers (numpy), device activations."""
+
+    def __init__(self, device: int = 0, fp16: bool = False):
+        h = _vp()
+        _check(lib().b200q8_backend_create(device, int(fp16), ctypes.byref(h)))
+        self.h = h
+        self.fp16 = fp16
+
+    def close(self):
+        if self.h:
+            lib().b200q8_backend_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream) -> None:
+        _check(lib().b200q8_backend_set_stream(self.h, _stream(stream)))
+
+    def cached_bytes(self) -> int:
+        n = _sz()
+        _check(lib().b200q8_backend_cached_bytes(self.h, ctypes.byref(n)))
+        return n.value
+
+    def linear_q8(self, out, inp, weight, scales, bias, M, N, K) -> None:
+        """out/inp: device tensors; weight/scales/bias: host numpy arrays (cache keys)."""
+        _check(lib().b200q8_backend_linear_q8(
+            self.h, _addr(out), _addr(inp), weight.ctypes.data, scales.ctypes.data,
+            None if bias is None else bias.ctypes.data, M, N, K))
+
+    def linear_q8_add(self, out, inp, weight, scales, bias, residual, M, N, K) -> None:
+        _check(lib().b200q8_backend_linear_q8_add(
+            self.h, _addr(out), _addr(inp), weight.ctypes.data, scales.ctypes.data,
+            None if bias is None else bias.ctypes.data, _addr(residual), M, N, K))
+
+    def quantize_per_channel(self, w):
+        """Host fp32 [N,K] -> (host int8 [N,K], host fp32 [N]), computed on the GPU."""
+        import numpy as np
+
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        N, K = w.shape
+        q = np.empty((N, K), dtype=np.int8)
+        s = np.empty((N,), dtype=np.float32)
+        _check(lib().b200q8_backend_quantize_per_channel(self.h, w.ctypes.data, N, K, q.ctypes.data,
+                                                         s.ctypes.data))
+        return q, s
+
+
+class Comm:
+    """NCCL communicator over the ranks of one node (non-blocking init with a deadline)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _check(lib().b200q8_comm_unique_id(buf))
+        return buf.raw
+
+    def __init__(self, device: int, nranks: int, rank: int, uid: bytes, timeout_s: float = 60.0):
+        assert len(uid) == 128
+        h = _vp()
+        _check(lib().b200q8_comm_init(device, nranks, rank, uid, timeout_s, ctypes.byref(h)))
+        self.h = h
+        self.nranks, self.rank = nranks, rank
+
+    def destroy(self) -> None:
+        if self.h:
+            h, self.h = self.h, None
+            _check(lib().b200q8_comm_destroy(h))
+
+    def allgather(self, buf, count: int, dtype: int, stream=None) -> None:
+        """In place: rank r's slice is buf[r*count:(r+1)*count]."""
+        _check(lib().b200q8_comm_allgather(self.h, _addr(buf), count, dtype, _stream(stream)))
+
+    def abort(self) -> None:
+        if self.h:
+            h, self.h = self.h, None
+            lib().b200q8_comm_abort(h)
+
+
+def linear_q8_sharded(comm: Comm, out, x, w_shard, scales_shard, bias_shard, N: int, gather=None,
+                      stream=None) -> None:
+    """out[M,N] (all ranks) = linear_q8 over the column-sharded weight, NCCL all-gathered."""
+    M, K = x.shape
+    _check(lib().b200q8_linear_q8_sharded(comm.h, _addr(out), _dtype_code(out), _addr(x),
+                                          _dtype_code(x), _addr(w_shard), _addr(scales_shard),
+                                          _addr(bias_shard), M, N, K, _addr(gather),
+                                          _stream(stream)))

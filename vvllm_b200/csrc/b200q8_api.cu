@@ -1,0 +1,627 @@
+// b200q8_api.cu -- the extern "C" boundary (include/b200q8.h) over the sm_100a kernels.
+//
+// Host C++20.  No entry point exits the process or falls back to the CPU:
+// every failure becomes a negative status plus a thread-local message.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+
+#include "../../include/b200q8.h"
+#include "kernels.h"
+
+namespace b200q8 {
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    return fail(B200Q8_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+    int num_sms = 0;
+    size_t max_smem = 0;  // opt-in dynamic shared memory per block
+    int cc_major = 0, cc_minor = 0;
+    bool valid = false;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo* out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(B200Q8_ERR_UNSUPPORTED, "device %d out of range", dev);
+    if (!g_dev[dev].valid) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if (!g_dev[dev].valid) {
+            DeviceInfo d;
+            int v = 0;
+            if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+                return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
+            if ((e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+                return cuda_fail(e, "cudaDeviceGetAttribute(smem)");
+            d.max_smem = (size_t)v;
+            cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+            cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+            d.valid = true;
+            g_dev[dev] = d;
+        }
+    }
+    *out = g_dev[dev];
+    if (out->cc_major != 10)
+        return fail(B200Q8_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only",
+                    dev, out->cc_major, out->cc_minor);
+    return B200Q8_OK;
+}
+
+bool valid_dtype(int d) { return d == B200Q8_F32 || d == B200Q8_F16; }
+
+int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
+                const float* scales, const float* bias, const void* residual, size_t M, size_t N,
+                size_t K, cudaStream_t stream)
+{
+    if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8: dtype must be B200Q8_F32 or B200Q8_F16");
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!out || !inp || !weight || !scales)
+        return fail(B200Q8_ERR_INVALID, "linear_q8: null out/inp/weight/scales");
+    if (K == 0) return fail(B200Q8_ERR_INVALID, "linear_q8: K == 0");
+    if (N > (size_t)INT32_MAX || K > (size_t)INT32_MAX || M > (size_t)INT32_MAX ||
+        N * K / K != N)
+        return fail(B200Q8_ERR_INVALID, "linear_q8: sizes overflow (M=%zu N=%zu K=%zu)", M, N, K);
+    const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4, ib = in_dtype == B200Q8_F16 ? 2 : 4;
+    {   // inp must not overlap out
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t i0 = (uintptr_t)inp, i1 = i0 + M * K * ib;
+        if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8: inp overlaps out");
+    }
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+
+    LinearArgs a;
+    a.x = inp;
+    a.w = weight;
+    a.scales = scales;
+    a.bias = bias;
+    a.res = residual;
+    a.out = out;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.in_dtype = in_dtype;
+    a.out_dtype = out_dtype;
+    a.pdl = true;
+    cudaError_t e;
+    if ((int)M > gemv_max_tokens() && gemm_tc_supports(a)) {
+        e = launch_q8_gemm_tc(a, d.num_sms, stream);
+        if (e == cudaSuccess) return B200Q8_OK;
+        if (e != cudaErrorNotSupported) return cuda_fail(e, "q8_gemm_tc launch");
+        cudaGetLastError();
+    }
+    if ((int)M <= gemv_max_tokens()) {
+        e = launch_q8_gemv(a, d.num_sms, d.max_smem, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "q8_gemv launch");
+        return B200Q8_OK;
+    }
+    // M beyond the GEMV's token count and not taken by the tensor-core GEMM:
+    // stream the weights once per group of up to 4 tokens.
+    const int mt = gemv_max_tokens();
+    for (size_t m0 = 0; m0 < M; m0 += (size_t)mt) {
+        LinearArgs b = a;
+        b.M = (M - m0 < (size_t)mt) ? (M - m0) : (size_t)mt;
+        b.x = (const char*)inp + m0 * K * ib;
+        b.out = (char*)out + m0 * N * ob;
+        b.res = residual ? (const char*)residual + m0 * N * ob : nullptr;
+        e = launch_q8_gemv(b, d.num_sms, d.max_smem, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "q8_gemv launch");
+    }
+    return B200Q8_OK;
+}
+
+}  // namespace
+}  // namespace b200q8
+
+using namespace b200q8;
+
+extern "C" {
+
+int b200q8_abi_version(void) { return B200Q8_ABI_VERSION; }
+
+const char* b200q8_last_error(void) { return t_last_error.c_str(); }
+
+uint64_t b200q8_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int b200q8_quantize_per_channel(const float* w, size_t N, size_t K, int8_t* q, float* scales,
+                                b200q8_stream_t stream)
+{
+    if (N == 0) return B200Q8_OK;
+    if (!w || !q || !scales) return fail(B200Q8_ERR_INVALID, "quantize: null pointer");
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(scales, 0, N * sizeof(float), stream);
+        return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    if (N > (size_t)INT32_MAX || K > ((size_t)1 << 40))
+        return fail(B200Q8_ERR_INVALID, "quantize: sizes overflow (N=%zu K=%zu)", N, K);
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+    cudaError_t e = launch_q8_quantize(w, N, K, q, scales, d.num_sms, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "q8_quantize launch");
+    return B200Q8_OK;
+}
+
+int b200q8_linear_q8(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
+                     const float* scales, const float* bias, size_t M, size_t N, size_t K,
+                     b200q8_stream_t stream)
+{
+    return linear_impl(out, out_dtype, inp, in_dtype, weight, scales, bias, nullptr, M, N, K,
+                       (cudaStream_t)stream);
+}
+
+int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype,
+                         const int8_t* weight, const float* scales, const float* bias,
+                         const void* residual, size_t M, size_t N, size_t K, b200q8_stream_t stream)
+{
+    if (!residual && M && N) return fail(B200Q8_ERR_INVALID, "linear_q8_add: null residual");
+    if (residual && residual != out && M && N) {
+        // residual must either be out itself or not overlap it
+        const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4;
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t r0 = (uintptr_t)residual, r1 = r0 + M * N * ob;
+        if (o0 < r1 && r0 < o1)
+            return fail(B200Q8_ERR_INVALID, "linear_q8_add: residual partially overlaps out");
+    }
+    return linear_impl(out, out_dtype, inp, in_dtype, weight, scales, bias, residual, M, N, K,
+                       (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Backend layer: host weight pointers cached on the device by host address.
+// Mirrors BackendCUDA::cache_weight (src/backend/backend_cuda.cc:51-59) --
+// first use uploads, later uses look up; entries live as long as the backend.
+// ===========================================================================
+struct b200q8_backend {
+    int device = 0;
+    bool fp16 = false;
+    cudaStream_t stream = nullptr;
+    struct Buf {
+        void* ptr;
+        size_t bytes;
+    };
+    std::unordered_map<const void*, Buf> cache;
+    size_t cached_bytes = 0;
+};
+
+namespace {
+
+int set_device(int dev)
+{
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    return B200Q8_OK;
+}
+
+int cache_upload(b200q8_backend* be, const void* host, size_t bytes, void** dptr)
+{
+    auto it = be->cache.find(host);
+    if (it != be->cache.end()) {
+        if (it->second.bytes < bytes)
+            return fail(B200Q8_ERR_INVALID,
+                        "weight cache: host pointer %p was first seen with %zu bytes, now %zu", host,
+                        it->second.bytes, bytes);
+        *dptr = it->second.ptr;
+        return B200Q8_OK;
+    }
+    void* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(B200Q8_ERR_ALLOC, "weight cache: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    // The host buffer is pageable model memory: a synchronous copy, once per weight.
+    e = cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(e, "weight cache: cudaMemcpy H2D");
+    }
+    be->cache.emplace(host, b200q8_backend::Buf{d, bytes});
+    be->cached_bytes += bytes;
+    *dptr = d;
+    return B200Q8_OK;
+}
+
+int backend_linear(b200q8_backend* be, float* out, const float* inp, const int8_t* weight,
+                   const float* scales, const float* bias, const float* residual, size_t M, size_t N,
+                   size_t K)
+{
+    if (!be) return fail(B200Q8_ERR_INVALID, "backend: null handle");
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!weight || !scales) return fail(B200Q8_ERR_INVALID, "backend: null weight/scales");
+    int st = set_device(be->device);
+    if (st) return st;
+    void *dw = nullptr, *ds = nullptr, *db = nullptr;
+    if ((st = cache_upload(be, weight, N * K, &dw))) return st;
+    if ((st = cache_upload(be, scales, N * sizeof(float), &ds))) return st;
+    if (bias && (st = cache_upload(be, bias, N * sizeof(float), &db))) return st;
+    const int dt = be->fp16 ? B200Q8_F16 : B200Q8_F32;
+    return linear_impl(out, dt, inp, dt, (const int8_t*)dw, (const float*)ds, (const float*)db,
+                       residual, M, N, K, be->stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200q8_backend_create(int device, int fp16, b200q8_backend** out)
+{
+    if (!out) return fail(B200Q8_ERR_INVALID, "backend_create: null out");
+    *out = nullptr;
+    int st = set_device(device);
+    if (st) return st;
+    DeviceInfo d;
+    if ((st = device_info(&d))) return st;
+    auto* be = new (std::nothrow) b200q8_backend();
+    if (!be) return fail(B200Q8_ERR_ALLOC, "backend_create: out of host memory");
+    be->device = device;
+    be->fp16 = fp16 != 0;
+    *out = be;
+    return B200Q8_OK;
+}
+
+int b200q8_backend_destroy(b200q8_backend* be)
+{
+    if (!be) return B200Q8_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(be->device);
+    for (auto& kv : be->cache) cudaFree(kv.second.ptr);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete be;
+    return B200Q8_OK;
+}
+
+int b200q8_backend_set_stream(b200q8_backend* be, b200q8_stream_t stream)
+{
+    if (!be) return fail(B200Q8_ERR_INVALID, "backend: null handle");
+    be->stream = (cudaStream_t)stream;
+    return B200Q8_OK;
+}
+
+int b200q8_backend_cached_bytes(const b200q8_backend* be, size_t* bytes)
+{
+    if (!be || !bytes) return fail(B200Q8_ERR_INVALID, "backend: null argument");
+    *bytes = be->cached_bytes;
+    return B200Q8_OK;
+}
+
+int b200q8_backend_linear_q8(b200q8_backend* be, float* out, const float* inp, const int8_t* weight,
+                             const float* scales, const float* bias, size_t M, size_t N, size_t K)
+{
+    return backend_linear(be, out, inp, weight, scales, bias, nullptr, M, N, K);
+}
+
+int b200q8_backend_linear_q8_add(b200q8_backend* be, float* out, const float* inp,
+                                 const int8_t* weight, const float* scales, const float* bias,
+                                 const float* residual, size_t M, size_t N, size_t K)
+{
+    if (!residual && M && N) return fail(B200Q8_ERR_INVALID, "linear_q8_add: null residual");
+    return backend_linear(be, out, inp, weight, scales, bias, residual, M, N, K);
+}
+
+int b200q8_backend_quantize_per_channel(b200q8_backend* be, const float* weight, size_t N, size_t K,
+                                        int8_t* q, float* scales)
+{
+    if (!be) return fail(B200Q8_ERR_INVALID, "backend: null handle");
+    if (N == 0) return B200Q8_OK;
+    if (!weight || !q || !scales) return fail(B200Q8_ERR_INVALID, "quantize: null pointer");
+    int st = set_device(be->device);
+    if (st) return st;
+    float* dw = nullptr;
+    int8_t* dq = nullptr;
+    float* ds = nullptr;
+    cudaError_t e;
+    const size_t nk = N * K;
+    if ((e = cudaMalloc(&dw, nk * sizeof(float) + 16)) != cudaSuccess ||
+        (e = cudaMalloc(&dq, nk + 16)) != cudaSuccess ||
+        (e = cudaMalloc(&ds, N * sizeof(float))) != cudaSuccess) {
+        cudaFree(dw);
+        cudaFree(dq);
+        cudaFree(ds);
+        cudaGetLastError();
+        return fail(B200Q8_ERR_ALLOC, "quantize: cudaMalloc: %s", cudaGetErrorString(e));
+    }
+    int rc = B200Q8_OK;
+    if ((e = cudaMemcpyAsync(dw, weight, nk * sizeof(float), cudaMemcpyHostToDevice, be->stream)) != cudaSuccess)
+        rc = cuda_fail(e, "quantize: H2D");
+    if (!rc) rc = b200q8_quantize_per_channel(dw, N, K, dq, ds, be->stream);
+    if (!rc && (e = cudaMemcpyAsync(q, dq, nk, cudaMemcpyDeviceToHost, be->stream)) != cudaSuccess)
+        rc = cuda_fail(e, "quantize: D2H q");
+    if (!rc && (e = cudaMemcpyAsync(scales, ds, N * sizeof(float), cudaMemcpyDeviceToHost, be->stream)) != cudaSuccess)
+        rc = cuda_fail(e, "quantize: D2H scales");
+    if (!rc && (e = cudaStreamSynchronize(be->stream)) != cudaSuccess) rc = cuda_fail(e, "quantize: sync");
+    cudaFree(dw);
+    cudaFree(dq);
+    cudaFree(ds);
+    return rc;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Sharded layer.  NCCL is resolved at run time (dlopen of libnccl.so.2): in a
+// process that already loaded NCCL (e.g. through torch.distributed) the same
+// library instance is reused; this library has no link-time NCCL dependency.
+// ===========================================================================
+namespace {
+
+struct NcclApi {
+    bool loaded = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi g_nccl;
+std::once_flag g_nccl_once;
+
+template <typename F>
+bool sym(void* h, const char* name, F* out)
+{
+    *out = reinterpret_cast<F>(dlsym(h, name));
+    return *out != nullptr;
+}
+
+const NcclApi& nccl()
+{
+    std::call_once(g_nccl_once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            g_nccl.why = std::string("dlopen(libnccl.so.2) failed: ") + dlerror();
+            return;
+        }
+        bool ok = sym(h, "ncclGetUniqueId", &g_nccl.GetUniqueId) &&
+                  sym(h, "ncclCommInitRankConfig", &g_nccl.CommInitRankConfig) &&
+                  sym(h, "ncclCommGetAsyncError", &g_nccl.CommGetAsyncError) &&
+                  sym(h, "ncclCommAbort", &g_nccl.CommAbort) &&
+                  sym(h, "ncclCommFinalize", &g_nccl.CommFinalize) &&
+                  sym(h, "ncclCommDestroy", &g_nccl.CommDestroy) &&
+                  sym(h, "ncclAllGather", &g_nccl.AllGather) &&
+                  sym(h, "ncclGetErrorString", &g_nccl.GetErrorString);
+        if (!ok) {
+            g_nccl.why = "libnccl.so.2 lacks a required symbol";
+            return;
+        }
+        g_nccl.loaded = true;
+    });
+    return g_nccl;
+}
+
+}  // namespace
+
+struct b200q8_comm {
+    ncclComm_t comm = nullptr;
+    int device = 0, nranks = 1, rank = 0;
+    double timeout_s = 60.0;
+};
+
+namespace {
+
+int nccl_fail(ncclResult_t r, const char* what)
+{
+    const char* s = nccl().GetErrorString ? nccl().GetErrorString(r) : "?";
+    return fail(B200Q8_ERR_NCCL, "%s: NCCL error %d (%s)", what, (int)r, s);
+}
+
+// Non-blocking communicators may answer ncclInProgress; poll until done or the deadline.
+int nccl_settle(b200q8_comm* c, ncclResult_t r, const char* what)
+{
+    if (r == ncclSuccess) return B200Q8_OK;
+    if (r != ncclInProgress) return nccl_fail(r, what);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t a = ncclInProgress;
+        ncclResult_t q = nccl().CommGetAsyncError(c->comm, &a);
+        if (q != ncclSuccess) return nccl_fail(q, "ncclCommGetAsyncError");
+        if (a == ncclSuccess) return B200Q8_OK;
+        if (a != ncclInProgress) return nccl_fail(a, what);
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > c->timeout_s) return fail(B200Q8_ERR_TIMEOUT, "%s: still in progress after %.1f s", what, el);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200q8_shard_range(size_t N, int nranks, int rank, size_t* row0, size_t* rows)
+{
+    if (nranks < 1 || rank < 0 || rank >= nranks || !row0 || !rows)
+        return fail(B200Q8_ERR_INVALID, "shard_range: bad rank %d of %d", rank, nranks);
+    const size_t per = (N + (size_t)nranks - 1) / (size_t)nranks;
+    const size_t a = per * (size_t)rank;
+    *row0 = a < N ? a : N;
+    *rows = a < N ? ((N - a) < per ? (N - a) : per) : 0;
+    return B200Q8_OK;
+}
+
+int b200q8_comm_unique_id(uint8_t id[128])
+{
+    if (!id) return fail(B200Q8_ERR_INVALID, "comm_unique_id: null id");
+    if (!nccl().loaded) return fail(B200Q8_ERR_NCCL, "%s", nccl().why.c_str());
+    ncclUniqueId u;
+    ncclResult_t r = nccl().GetUniqueId(&u);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    memcpy(id, &u, 128);
+    return B200Q8_OK;
+}
+
+int b200q8_comm_init(int device, int nranks, int rank, const uint8_t id[128], double timeout_s,
+                     b200q8_comm** out)
+{
+    if (!out || !id || nranks < 1 || rank < 0 || rank >= nranks)
+        return fail(B200Q8_ERR_INVALID, "comm_init: bad arguments");
+    *out = nullptr;
+    if (!nccl().loaded) return fail(B200Q8_ERR_NCCL, "%s", nccl().why.c_str());
+    int st = set_device(device);
+    if (st) return st;
+    auto* c = new (std::nothrow) b200q8_comm();
+    if (!c) return fail(B200Q8_ERR_ALLOC, "comm_init: out of host memory");
+    c->device = device;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
+    ncclUniqueId u;
+    memcpy(&u, id, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = nccl().CommInitRankConfig(&c->comm, nranks, u, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        int rc = nccl_fail(r, "ncclCommInitRankConfig");
+        delete c;
+        return rc;
+    }
+    st = nccl_settle(c, r, "ncclCommInitRankConfig");
+    if (st) {
+        std::string msg = t_last_error;
+        if (c->comm) nccl().CommAbort(c->comm);
+        delete c;
+        t_last_error = msg;
+        return st;
+    }
+    *out = c;
+    return B200Q8_OK;
+}
+
+int b200q8_comm_abort(b200q8_comm* c)
+{
+    if (!c) return B200Q8_OK;
+    if (c->comm && nccl().loaded) nccl().CommAbort(c->comm);
+    delete c;
+    return B200Q8_OK;
+}
+
+int b200q8_comm_destroy(b200q8_comm* c)
+{
+    if (!c) return B200Q8_OK;
+    int rc = B200Q8_OK;
+    if (c->comm && nccl().loaded) {
+        ncclResult_t r = nccl().CommFinalize(c->comm);
+        rc = nccl_settle(c, r, "ncclCommFinalize");
+        if (rc) {
+            nccl().CommAbort(c->comm);
+        } else {
+            r = nccl().CommDestroy(c->comm);
+            if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommDestroy");
+        }
+    }
+    delete c;
+    return rc;
+}
+
+int b200q8_comm_allgather(b200q8_comm* c, void* buf, size_t count, int dtype, b200q8_stream_t stream)
+{
+    if (!c || !buf) return fail(B200Q8_ERR_INVALID, "comm_allgather: null argument");
+    if (!valid_dtype(dtype)) return fail(B200Q8_ERR_INVALID, "comm_allgather: bad dtype");
+    if (!nccl().loaded) return fail(B200Q8_ERR_NCCL, "%s", nccl().why.c_str());
+    const size_t eb = dtype == B200Q8_F16 ? 2 : 4;
+    ncclResult_t r = nccl().AllGather((char*)buf + (size_t)c->rank * count * eb, buf, count,
+                                      dtype == B200Q8_F16 ? ncclFloat16 : ncclFloat32, c->comm,
+                                      (cudaStream_t)stream);
+    return nccl_settle(c, r, "ncclAllGather");
+}
+
+int b200q8_linear_q8_sharded(b200q8_comm* c, void* out, int out_dtype, const void* inp, int in_dtype,
+                             const int8_t* w_shard, const float* scales_shard, const float* bias_shard,
+                             size_t M, size_t N, size_t K, void* gather, b200q8_stream_t stream)
+{
+    if (!c) return fail(B200Q8_ERR_INVALID, "linear_q8_sharded: null comm");
+    if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8_sharded: bad dtype");
+    if (M == 0 || N == 0) return B200Q8_OK;
+    const size_t G = (size_t)c->nranks;
+    size_t row0 = 0, rows = 0;
+    int st = b200q8_shard_range(N, c->nranks, c->rank, &row0, &rows);
+    if (st) return st;
+    const size_t per = (N + G - 1) / G;  // padded shard width
+    const size_t eb = out_dtype == B200Q8_F16 ? 2 : 4;
+    const ncclDataType_t nt = out_dtype == B200Q8_F16 ? ncclFloat16 : ncclFloat32;
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool direct = (M == 1) && (N % G == 0);
+    if (!direct && !gather)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_sharded: gather scratch required (M=%zu, N %% G = %zu)",
+                    M, N % G);
+    // local slice: [M, rows] with row stride `per` inside the rank's gather slot
+    char* slot = direct ? (char*)out + (size_t)c->rank * per * eb
+                        : (char*)gather + (size_t)c->rank * M * per * eb;
+    if (rows > 0) {
+        if (M == 1 || rows == per) {
+            st = linear_impl(slot, out_dtype, inp, in_dtype, w_shard, scales_shard, bias_shard, nullptr,
+                             M, rows, K, s);
+        } else {
+            // tail rank with fewer rows: compute each token row separately into the padded slot
+            for (size_t m = 0; m < M && !st; m++)
+                st = linear_impl(slot + m * per * eb, out_dtype, (const char*)inp + m * K * (in_dtype == B200Q8_F16 ? 2 : 4),
+                                 in_dtype, w_shard, scales_shard, bias_shard, nullptr, 1, rows, K, s);
+        }
+        if (st) return st;
+    }
+    if (!nccl().loaded) return fail(B200Q8_ERR_NCCL, "%s", nccl().why.c_str());
+    void* recv = direct ? out : gather;
+    ncclResult_t r = nccl().AllGather(slot, recv, M * per, nt, c->comm, s);
+    st = nccl_settle(c, r, "ncclAllGather");
+    if (st) return st;
+    if (!direct) {
+        cudaError_t e = launch_gather_permute(gather, out, (int)eb, G, M, per, N, s);
+        if (e != cudaSuccess) return cuda_fail(e, "gather permute launch");
+    }
+    return B200Q8_OK;
+}
+
+}  // extern "C"

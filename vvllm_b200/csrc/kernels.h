@@ -1,0 +1,46 @@
+// kernels.h -- internal launch interface between the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200q8 {
+
+enum DType : int { kF32 = 0, kF16 = 1 };
+
+struct LinearArgs {
+    const void* x = nullptr;        // [M, K] activations (in_dtype)
+    const int8_t* w = nullptr;      // [N, K] int8, row-major
+    const float* scales = nullptr;  // [N]
+    const float* bias = nullptr;    // [N] or null
+    const void* res = nullptr;      // [M, N] residual (out_dtype) or null
+    void* out = nullptr;            // [M, N] (out_dtype)
+    size_t M = 0, N = 0, K = 0;
+    int in_dtype = kF32, out_dtype = kF32;
+    bool pdl = false;               // launch with programmatic stream serialization
+};
+
+// Streaming SIMT GEMV, M <= gemv_max_tokens().  Also takes any M/K through a
+// generic (slow, correct) kernel when the fast one cannot (alignment, K % 16).
+cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cudaStream_t stream);
+int gemv_max_tokens();
+size_t gemv_smem_bytes(int M, int K);
+
+// Per-row absmax quantization (bit-exact with vvllm::quantize_per_channel).
+cudaError_t launch_q8_quantize(const float* w, size_t N, size_t K, int8_t* q, float* scales,
+                               int num_sms, cudaStream_t stream);
+
+// tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (the prefill and skinny path).
+// Returns cudaErrorNotSupported when the shape is outside what it takes.
+cudaError_t launch_q8_gemm_tc(const LinearArgs& a, int num_sms, cudaStream_t stream);
+bool gemm_tc_supports(const LinearArgs& a);
+
+// [G][M][Ns] (rank-major gather result) -> [M][N] (N = true width, Ns = padded shard width)
+cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, size_t G, size_t M,
+                                  size_t Ns, size_t N, cudaStream_t stream);
+
+// Counts every kernel launch made by this library (for the bench's launch count).
+void note_launch();
+
+}  // namespace b200q8
