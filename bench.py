@@ -214,6 +214,30 @@ def run_reference(args):
     return 0
 
 
+def profile_case(args):
+    """Small single-projection run for ncu: warmup + 1 launches of one linear_q8 on one GPU.
+    Weights are random int8 made with one torch launch (values do not change the memory traffic)."""
+    import torch
+
+    import vvllm_b200 as v
+
+    name, _, m = args.profile_case.partition(":")
+    M = int(m) if m else 1
+    N, K = {n: (N, K) for n, N, K in PROJ}[name]
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+    s = torch.rand(N, device=dev) * 1e-3
+    x = torch.randn(M, K, device=dev).half()
+    out = torch.empty(M, N, device=dev, dtype=torch.float16)
+    for _ in range(args.warmup + 1):
+        v.linear_q8(out, x, q, s)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "M": M, "N": N, "K": K,
+                      "algorithmic_bytes": algo_bytes(N, K, M), "launches": args.warmup + 1}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -224,11 +248,15 @@ def main():
                     help="fraction of each projection's rows timed on the CPU")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None,
+                    help="run one projection (gate_up|down|lm_head, optional :M) warmup+1 times for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_case:
+        return profile_case(args)
 
     import torch
     import torch.distributed as dist

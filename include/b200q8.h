@@ -87,6 +87,24 @@ B200Q8_API int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, i
                          const void* residual, size_t M, size_t N, size_t K,
                          b200q8_stream_t stream);
 
+/* Kernel choice for b200q8_linear_q8_ex. */
+#define B200Q8_ALGO_AUTO 0 /* fp16 activations -> tensor cores; fp32 -> SIMT GEMV */
+#define B200Q8_ALGO_SIMT 1 /* streaming SIMT GEMV (any dtype; groups of <= 4 tokens) */
+#define B200Q8_ALGO_TC 2   /* tcgen05 kernel (fp16 activations, K % 16 == 0, aligned) */
+
+/* Both of the above in one call (residual may be NULL) with an explicit
+ * kernel choice; B200Q8_ERR_UNSUPPORTED if the chosen kernel cannot take the
+ * shape.  Same semantics as b200q8_linear_q8 / b200q8_linear_q8_add. */
+B200Q8_API int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, int in_dtype,
+                                   const int8_t* weight, const float* scales, const float* bias,
+                                   const void* residual, size_t M, size_t N, size_t K, int algo,
+                                   b200q8_stream_t stream);
+
+/* Device error word of the current device: bit 0 is set when a bounded wait
+ * inside the tensor-core kernel gave up (its outputs are then invalid).
+ * clear != 0 resets it.  Synchronises with the device. */
+B200Q8_API int b200q8_kernel_error(int* code, int clear);
+
 /* ------------------------------------------------------------------------
  * 2. Backend layer.  Mirrors vvllm::BackendCUDA's hot-path conventions:
  *    activations (out, inp, residual) are device pointers, fp32 or -- when the

@@ -24,8 +24,10 @@ def _t(a, dev, dtype=None):
     return t if dtype is None else t.to(dtype)
 
 
-def run_gpu(cuda, x, q, s, b=None, res=None, in16=False, out16=False, inplace=False):
-    """Runs the kernel; returns (y as fp32 numpy, oracle inputs x_eff, res_eff)."""
+def run_gpu(cuda, x, q, s, b=None, res=None, in16=False, out16=False, inplace=False, algo=None):
+    """Runs the kernel; returns (y as fp32 numpy, oracle inputs x_eff, res_eff).
+    algo=None goes through b200q8_linear_q8 / _add (automatic kernel choice);
+    otherwise b200q8_linear_q8_ex with that kernel."""
     import torch
 
     import vvllm_b200 as v
@@ -35,16 +37,22 @@ def run_gpu(cuda, x, q, s, b=None, res=None, in16=False, out16=False, inplace=Fa
     bt = _t(b, cuda) if b is not None else None
     odt = torch.float16 if out16 else torch.float32
     M, N = x.shape[0], q.shape[0]
+    rt = None
     if res is not None:
         rt = _t(res, cuda, odt)
         res_eff = rt.float().cpu().numpy()
         out = rt if inplace else torch.empty((M, N), dtype=odt, device=cuda)
-        v.linear_q8_add(out, xt, qt, st, bt, rt)
     else:
         res_eff = None
         out = torch.empty((M, N), dtype=odt, device=cuda)
+    if algo is not None:
+        v.linear_q8_ex(out, xt, qt, st, bt, rt, algo=algo)
+    elif rt is not None:
+        v.linear_q8_add(out, xt, qt, st, bt, rt)
+    else:
         v.linear_q8(out, xt, qt, st, bt)
     torch.cuda.synchronize()
+    assert v.kernel_error() == 0
     x_eff = xt.float().cpu().numpy()
     return out.float().cpu().numpy(), x_eff, res_eff
 
@@ -94,6 +102,61 @@ def test_linear_shapes(cuda, oracle, name, M, N, K, in16, out16):
     tol = TOL_F16 if (in16 or out16) else TOL_F32
     err = rowwise_normwise_err(y, ref)
     assert err <= tol, err
+
+
+TC_SHAPES = [
+    # name, M, N, K -- the tensor-core kernel across token tiles (BN 16..256) and ragged edges
+    ("tc_m1", 1, 4864, 896), ("tc_m1_k3584", 1, 1000, 3584), ("tc_m3", 3, 640, 576),
+    ("tc_m16", 16, 384, 1536), ("tc_m17", 17, 300, 896), ("tc_m32", 32, 256, 4864),
+    ("tc_m40", 40, 130, 896), ("tc_m64", 64, 512, 3584), ("tc_m100", 100, 200, 1536),
+    ("tc_m128", 128, 256, 896), ("tc_m200", 200, 129, 576), ("tc_m300", 300, 384, 896),
+    ("tc_k_tail", 8, 256, 16 * 37), ("tc_n1", 5, 1, 896), ("tc_n127", 2, 127, 128),
+]
+
+
+@pytest.mark.parametrize("out16", [True, False])
+@pytest.mark.parametrize("algo_name", ["simt", "tc"])
+@pytest.mark.parametrize("name,M,N,K", TC_SHAPES)
+def test_fp16_paths_explicit(cuda, oracle, name, M, N, K, algo_name, out16):
+    """Both kernels on the fp16-activation path, called explicitly, against the oracle."""
+    import vvllm_b200 as v
+
+    if algo_name == "simt" and M > 40:
+        pytest.skip("SIMT path streams W once per 4 tokens: covered at small M")
+    algo = v.ALGO_TC if algo_name == "tc" else v.ALGO_SIMT
+    w = make_weight(N, K, zlib.crc32(name.encode()) % 1000 + 3)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 77)
+    b = make_bias(N, 78)
+    res = make_x(M, N, 79) if M % 2 else None
+    y, xe, re = run_gpu(cuda, x, q, s, b, res, in16=True, out16=out16, inplace=res is not None, algo=algo)
+    ref = oracle_ref(oracle, xe, q, s, b, re)
+    assert rowwise_normwise_err(y, ref) <= TOL_F16
+
+
+PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs
+
+
+@pytest.mark.parametrize("K,N", PREFILL)
+def test_prefill_config4(cuda, oracle, K, N):
+    """M = 512 tokens, fp16 in / fp16 out, int8 per-row weights (config 4); sampled rows checked."""
+    import torch
+
+    import vvllm_b200 as v
+
+    M = 512
+    w = make_weight(N, K, 500 + N)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 501)
+    xt = torch.from_numpy(x).to(cuda).half()
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    v.linear_q8(out, xt, torch.from_numpy(q).to(cuda), torch.from_numpy(s).to(cuda))
+    torch.cuda.synchronize()
+    assert v.kernel_error() == 0
+    rows = sample_rows(N, 256)
+    ref = oracle.linear_q8(xt.float().cpu().numpy(), q[rows], s[rows], None)
+    y = out.float().cpu().numpy()[:, rows]
+    assert rowwise_normwise_err(y, ref) <= TOL_F16
 
 
 @pytest.mark.parametrize("in16", [False, True])

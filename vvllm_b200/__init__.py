@@ -16,6 +16,11 @@ from ._lib import (  # noqa: F401
     launch_count,
     linear_q8,
     linear_q8_add,
+    linear_q8_ex,
+    kernel_error,
+    ALGO_AUTO,
+    ALGO_SIMT,
+    ALGO_TC,
     linear_q8_sharded,
     quantize_per_channel,
     shard_range,

@@ -34,6 +34,8 @@ _SIGS = {
     "b200q8_quantize_per_channel": ([_vp, _sz, _sz, _vp, _vp, _vp], _int),
     "b200q8_linear_q8": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_linear_q8_ex": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _int, _vp], _int),
+    "b200q8_kernel_error": ([ctypes.POINTER(_int), _int], _int),
     "b200q8_backend_create": ([_int, _int, ctypes.POINTER(_vp)], _int),
     "b200q8_backend_destroy": ([_vp], _int),
     "b200q8_backend_set_stream": ([_vp, _vp], _int),
@@ -129,6 +131,25 @@ def linear_q8_add(out, x, w, scales, bias, residual, stream=None) -> None:
     _check(lib().b200q8_linear_q8_add(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x),
                                       _addr(w), _addr(scales), _addr(bias), _addr(residual), M, N,
                                       K, _stream(stream)))
+
+
+ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
+
+
+def linear_q8_ex(out, x, w, scales, bias=None, residual=None, algo=ALGO_AUTO, stream=None) -> None:
+    """linear_q8 / linear_q8_add with an explicit kernel choice (ALGO_SIMT / ALGO_TC)."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib().b200q8_linear_q8_ex(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x), _addr(w),
+                                     _addr(scales), _addr(bias), _addr(residual), M, N, K, algo,
+                                     _stream(stream)))
+
+
+def kernel_error(clear: bool = True) -> int:
+    """Device error word (bit 0: a bounded wait in the tensor-core kernel gave up)."""
+    c = _int()
+    _check(lib().b200q8_kernel_error(ctypes.byref(c), int(clear)))
+    return c.value
 
 
 def shard_range(N: int, nranks: int, rank: int) -> tuple[int, int]:

@@ -18,7 +18,7 @@
 #include <thread>
 #include <unordered_map>
 
-#include "../../include/b200q8.h"
+#include "b200q8.h"
 #include "kernels.h"
 
 namespace b200q8 {
@@ -88,10 +88,84 @@ int device_info(DeviceInfo* out)
 
 bool valid_dtype(int d) { return d == B200Q8_F32 || d == B200Q8_F16; }
 
+// Stream-K scratch of the tensor-core GEMM, one per (device, stream): launches
+// on one stream are ordered, so they may share it; different streams may run
+// concurrently, so they do not.  Allocated on first use (outside any graph
+// capture) and grown when a larger shape needs more; never shrunk.
+struct ScratchKey {
+    int dev;
+    cudaStream_t stream;
+    bool operator==(const ScratchKey& o) const { return dev == o.dev && stream == o.stream; }
+};
+struct ScratchKeyHash {
+    size_t operator()(const ScratchKey& k) const
+    {
+        return std::hash<uintptr_t>()((uintptr_t)k.stream) * 31u + (size_t)k.dev;
+    }
+};
+std::mutex g_scratch_mu;
+std::unordered_map<ScratchKey, TcScratch, ScratchKeyHash> g_scratch;
+
+int get_scratch(const LinearArgs& a, int num_sms, cudaStream_t stream, TcScratch* out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    size_t need_ws = 0, need_cnt = 0;
+    gemm_tc_scratch_need(a, num_sms, &need_ws, &need_cnt);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    TcScratch& s = g_scratch[ScratchKey{dev, stream}];
+    if (s.ws_floats < need_ws || s.counters < need_cnt) {
+        // Default capacity covers 128-token tiles on every SM and 64K tiles.
+        size_t ws = s.ws_floats, cnt = s.counters;
+        const size_t def_ws = (size_t)2 * num_sms * 128 * 128, def_cnt = (size_t)1 << 16;
+        if (ws < need_ws) ws = need_ws > def_ws ? need_ws : def_ws;
+        if (cnt < need_cnt) cnt = need_cnt > def_cnt ? need_cnt : def_cnt;
+        float* nws = nullptr;
+        int* ncnt = nullptr;
+        if ((e = cudaMalloc(&nws, ws * sizeof(float))) != cudaSuccess ||
+            (e = cudaMalloc(&ncnt, cnt * sizeof(int))) != cudaSuccess) {
+            cudaFree(nws);
+            cudaGetLastError();
+            return fail(B200Q8_ERR_ALLOC, "tensor-core scratch: cudaMalloc: %s", cudaGetErrorString(e));
+        }
+        if ((e = cudaMemsetAsync(ncnt, 0, cnt * sizeof(int), stream)) != cudaSuccess) {
+            cudaFree(nws);
+            cudaFree(ncnt);
+            return cuda_fail(e, "tensor-core scratch: memset");
+        }
+        if (s.ws) {  // old buffers may still be read by queued work on this stream
+            cudaStreamSynchronize(stream);
+            cudaFree(s.ws);
+            cudaFree(s.counter_ptr);
+        }
+        s.ws = nws;
+        s.ws_floats = ws;
+        s.counter_ptr = ncnt;
+        s.counters = cnt;
+    }
+    *out = s;
+    return B200Q8_OK;
+}
+
+// After a bounded wait gave up, tile counters may be left non-zero: reset them.
+int reset_scratch_counters(int dev)
+{
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    for (auto& kv : g_scratch) {
+        if (kv.first.dev != dev || !kv.second.counter_ptr) continue;
+        cudaError_t e = cudaMemset(kv.second.counter_ptr, 0, kv.second.counters * sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e, "reset scratch counters");
+    }
+    return B200Q8_OK;
+}
+
 int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
                 const float* scales, const float* bias, const void* residual, size_t M, size_t N,
-                size_t K, cudaStream_t stream)
+                size_t K, cudaStream_t stream, int algo = B200Q8_ALGO_AUTO)
 {
+    if (algo != B200Q8_ALGO_AUTO && algo != B200Q8_ALGO_SIMT && algo != B200Q8_ALGO_TC)
+        return fail(B200Q8_ERR_INVALID, "linear_q8: unknown algo %d", algo);
     if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
         return fail(B200Q8_ERR_INVALID, "linear_q8: dtype must be B200Q8_F32 or B200Q8_F16");
     if (M == 0 || N == 0) return B200Q8_OK;
@@ -125,11 +199,18 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     a.out_dtype = out_dtype;
     a.pdl = true;
     cudaError_t e;
-    if ((int)M > gemv_max_tokens() && gemm_tc_supports(a)) {
-        e = launch_q8_gemm_tc(a, d.num_sms, stream);
-        if (e == cudaSuccess) return B200Q8_OK;
-        if (e != cudaErrorNotSupported) return cuda_fail(e, "q8_gemm_tc launch");
-        cudaGetLastError();
+    // fp16 activations: the tensor-core kernel for every M; fp32 activations: the SIMT GEMV.
+    const bool tc_ok = gemm_tc_supports(a);
+    if (algo == B200Q8_ALGO_TC && !tc_ok)
+        return fail(B200Q8_ERR_UNSUPPORTED,
+                    "linear_q8: tensor-core path needs fp16 activations, K %% 16 == 0 and 16-byte aligned "
+                    "weight/activation pointers (in_dtype=%d K=%zu)", in_dtype, K);
+    if (tc_ok && algo != B200Q8_ALGO_SIMT) {
+        TcScratch scratch;
+        if ((st = get_scratch(a, d.num_sms, stream, &scratch))) return st;
+        e = launch_q8_gemm_tc(a, d.num_sms, scratch, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "q8_gemm_tc launch");
+        return B200Q8_OK;
     }
     if ((int)M <= gemv_max_tokens()) {
         e = launch_q8_gemv(a, d.num_sms, d.max_smem, stream);
@@ -189,6 +270,34 @@ int b200q8_linear_q8(void* out, int out_dtype, const void* inp, int in_dtype, co
 {
     return linear_impl(out, out_dtype, inp, in_dtype, weight, scales, bias, nullptr, M, N, K,
                        (cudaStream_t)stream);
+}
+
+int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
+                        const float* scales, const float* bias, const void* residual, size_t M, size_t N,
+                        size_t K, int algo, b200q8_stream_t stream)
+{
+    if (residual && residual != out && M && N) {
+        const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4;
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t r0 = (uintptr_t)residual, r1 = r0 + M * N * ob;
+        if (o0 < r1 && r0 < o1)
+            return fail(B200Q8_ERR_INVALID, "linear_q8_ex: residual partially overlaps out");
+    }
+    return linear_impl(out, out_dtype, inp, in_dtype, weight, scales, bias, residual, M, N, K,
+                       (cudaStream_t)stream, algo);
+}
+
+int b200q8_kernel_error(int* code, int clear)
+{
+    if (!code) return fail(B200Q8_ERR_INVALID, "kernel_error: null code");
+    cudaError_t e = read_kernel_error(code, clear != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel_error: read device word");
+    if (clear && *code) {
+        int dev = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+        return reset_scratch_counters(dev);
+    }
+    return B200Q8_OK;
 }
 
 int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype,

@@ -31,10 +31,26 @@ size_t gemv_smem_bytes(int M, int K);
 cudaError_t launch_q8_quantize(const float* w, size_t N, size_t K, int8_t* q, float* scales,
                                int num_sms, cudaStream_t stream);
 
-// tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (the prefill and skinny path).
-// Returns cudaErrorNotSupported when the shape is outside what it takes.
-cudaError_t launch_q8_gemm_tc(const LinearArgs& a, int num_sms, cudaStream_t stream);
+// Scratch of the stream-K tensor-core GEMM: fp32 partial accumulators of split
+// tiles and per-tile arrival counters (zero between launches; every launch
+// leaves them zero unless a bounded wait gave up).
+struct TcScratch {
+    float* ws = nullptr;
+    size_t ws_floats = 0;
+    int* counter_ptr = nullptr;
+    size_t counters = 0;
+};
+
+// tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (decode, skinny and prefill).
+// Returns cudaErrorNotSupported when the shape is outside what it takes and
+// cudaErrorMemoryAllocation when `scratch` is smaller than gemm_tc_scratch_need says.
+cudaError_t launch_q8_gemm_tc(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream);
 bool gemm_tc_supports(const LinearArgs& a);
+void gemm_tc_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters);
+
+// Reads (and optionally clears) the device error word the tensor-core kernel
+// sets when a bounded wait gives up (bit 0).
+cudaError_t read_kernel_error(int* code, bool clear);
 
 // [G][M][Ns] (rank-major gather result) -> [M][N] (N = true width, Ns = padded shard width)
 cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, size_t G, size_t M,
