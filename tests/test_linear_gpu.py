@@ -115,15 +115,15 @@ TC_SHAPES = [
 
 
 @pytest.mark.parametrize("out16", [True, False])
-@pytest.mark.parametrize("algo_name", ["simt", "tc"])
+@pytest.mark.parametrize("algo_name", ["simt", "tc", "tc_i8"])
 @pytest.mark.parametrize("name,M,N,K", TC_SHAPES)
 def test_fp16_paths_explicit(cuda, oracle, name, M, N, K, algo_name, out16):
-    """Both kernels on the fp16-activation path, called explicitly, against the oracle."""
+    """Every kernel on the fp16-activation path, called explicitly, against the oracle."""
     import vvllm_b200 as v
 
     if algo_name == "simt" and M > 40:
         pytest.skip("SIMT path streams W once per 4 tokens: covered at small M")
-    algo = v.ALGO_TC if algo_name == "tc" else v.ALGO_SIMT
+    algo = {"simt": v.ALGO_SIMT, "tc": v.ALGO_TC, "tc_i8": v.ALGO_TC_I8}[algo_name]
     w = make_weight(N, K, zlib.crc32(name.encode()) % 1000 + 3)
     q, s = oracle.quantize_per_channel(w)
     x = make_x(M, K, 77)
@@ -132,6 +132,60 @@ def test_fp16_paths_explicit(cuda, oracle, name, M, N, K, algo_name, out16):
     y, xe, re = run_gpu(cuda, x, q, s, b, res, in16=True, out16=out16, inplace=res is not None, algo=algo)
     ref = oracle_ref(oracle, xe, q, s, b, re)
     assert rowwise_normwise_err(y, ref) <= TOL_F16
+
+
+I8_FP32_SHAPES = [
+    # fp32 activations on the int8 tensor-core kernel: exact digits must hold the 1e-5 bar
+    ("i8_m1", 1, 4864, 896), ("i8_m1_k4864", 1, 896, 4864), ("i8_m2", 2, 300, 576), ("i8_m4", 4, 1536, 576),
+    ("i8_m5", 5, 200, 1536), ("i8_m16", 16, 640, 896), ("i8_m33", 33, 256, 3584), ("i8_m64", 64, 130, 896),
+    ("i8_m100", 100, 128, 576), ("i8_k16", 3, 50, 16), ("i8_k18944", 1, 448, 18944),
+]
+
+
+@pytest.mark.parametrize("name,M,N,K", I8_FP32_SHAPES)
+def test_i8_digits_fp32(cuda, oracle, name, M, N, K):
+    import vvllm_b200 as v
+
+    w = make_weight(N, K, zlib.crc32(name.encode()) % 1000 + 5)
+    q, s = oracle.quantize_per_channel(w)
+    x = make_x(M, K, 81) * np.float32(3.0)
+    b = make_bias(N, 82)
+    res = make_x(M, N, 83) if M % 2 else None
+    y, xe, re = run_gpu(cuda, x, q, s, b, res, inplace=res is not None, algo=v.ALGO_TC_I8)
+    assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, re)) <= TOL_F32
+
+
+def test_i8_digits_wide_dynamic_range(cuda, oracle):
+    """Activations spanning many binades (tiny, huge, zero rows) keep the fp32 tolerance."""
+    import vvllm_b200 as v
+
+    N, K, M = 384, 1536, 4
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 91))
+    x = make_x(M, K, 92)
+    x[0] *= np.float32(1e-30)
+    x[1] *= np.float32(1e30)
+    x[2] = 0.0
+    x[3, ::7] *= np.float32(1e4)
+    y, xe, _ = run_gpu(cuda, x, q, s, None, None, algo=v.ALGO_TC_I8)
+    ref = oracle_ref(oracle, xe, q, s, None, None)
+    assert np.all(y[2] == 0.0)
+    for i in (0, 1, 3):
+        assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32, i
+
+
+def test_i8_nonfinite_rows_give_nan(cuda, oracle):
+    """A token row holding Inf/NaN yields NaN outputs on the digit kernel; other rows are exact."""
+    import vvllm_b200 as v
+
+    N, K = 256, 896
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 93))
+    x = make_x(3, K, 94)
+    x[1, 5] = np.inf
+    y, xe, _ = run_gpu(cuda, x, q, s, None, None, algo=v.ALGO_TC_I8)
+    assert np.all(np.isnan(y[1]))
+    ref = oracle_ref(oracle, xe, q, s, None, None)
+    for i in (0, 2):
+        assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32
 
 
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs

@@ -21,6 +21,7 @@ from ._lib import (  # noqa: F401
     ALGO_AUTO,
     ALGO_SIMT,
     ALGO_TC,
+    ALGO_TC_I8,
     linear_q8_sharded,
     quantize_per_channel,
     shard_range,

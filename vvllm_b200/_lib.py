@@ -133,7 +133,7 @@ def linear_q8_add(out, x, w, scales, bias, residual, stream=None) -> None:
                                       K, _stream(stream)))
 
 
-ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
+ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_TC_I8 = 0, 1, 2, 3
 
 
 def linear_q8_ex(out, x, w, scales, bias=None, residual=None, algo=ALGO_AUTO, stream=None) -> None:

@@ -106,44 +106,49 @@ struct ScratchKeyHash {
 std::mutex g_scratch_mu;
 std::unordered_map<ScratchKey, TcScratch, ScratchKeyHash> g_scratch;
 
-int get_scratch(const LinearArgs& a, int num_sms, cudaStream_t stream, TcScratch* out)
+struct ScratchNeed {
+    size_t ws = 0, counters = 0, dig = 0, exps = 0;
+};
+
+// Grows one device buffer of `s` to at least `need` elements (never shrinks).
+template <typename T>
+int grow(T** buf, size_t* have, size_t need, size_t dflt, cudaStream_t stream, bool zero, const char* what)
+{
+    if (*have >= need) return B200Q8_OK;
+    const size_t n = need > dflt ? need : dflt;
+    T* nb = nullptr;
+    cudaError_t e = cudaMalloc(&nb, n * sizeof(T));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(B200Q8_ERR_ALLOC, "scratch %s: cudaMalloc(%zu): %s", what, n * sizeof(T), cudaGetErrorString(e));
+    }
+    if (zero && (e = cudaMemsetAsync(nb, 0, n * sizeof(T), stream)) != cudaSuccess) {
+        cudaFree(nb);
+        return cuda_fail(e, "scratch memset");
+    }
+    if (*buf) {  // the old buffer may still be in use by queued work on this stream
+        cudaStreamSynchronize(stream);
+        cudaFree(*buf);
+    }
+    *buf = nb;
+    *have = n;
+    return B200Q8_OK;
+}
+
+int get_scratch(const ScratchNeed& need, int num_sms, cudaStream_t stream, TcScratch* out)
 {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    size_t need_ws = 0, need_cnt = 0;
-    gemm_tc_scratch_need(a, num_sms, &need_ws, &need_cnt);
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     TcScratch& s = g_scratch[ScratchKey{dev, stream}];
-    if (s.ws_floats < need_ws || s.counters < need_cnt) {
-        // Default capacity covers 128-token tiles on every SM and 64K tiles.
-        size_t ws = s.ws_floats, cnt = s.counters;
-        const size_t def_ws = (size_t)2 * num_sms * 128 * 128, def_cnt = (size_t)1 << 16;
-        if (ws < need_ws) ws = need_ws > def_ws ? need_ws : def_ws;
-        if (cnt < need_cnt) cnt = need_cnt > def_cnt ? need_cnt : def_cnt;
-        float* nws = nullptr;
-        int* ncnt = nullptr;
-        if ((e = cudaMalloc(&nws, ws * sizeof(float))) != cudaSuccess ||
-            (e = cudaMalloc(&ncnt, cnt * sizeof(int))) != cudaSuccess) {
-            cudaFree(nws);
-            cudaGetLastError();
-            return fail(B200Q8_ERR_ALLOC, "tensor-core scratch: cudaMalloc: %s", cudaGetErrorString(e));
-        }
-        if ((e = cudaMemsetAsync(ncnt, 0, cnt * sizeof(int), stream)) != cudaSuccess) {
-            cudaFree(nws);
-            cudaFree(ncnt);
-            return cuda_fail(e, "tensor-core scratch: memset");
-        }
-        if (s.ws) {  // old buffers may still be read by queued work on this stream
-            cudaStreamSynchronize(stream);
-            cudaFree(s.ws);
-            cudaFree(s.counter_ptr);
-        }
-        s.ws = nws;
-        s.ws_floats = ws;
-        s.counter_ptr = ncnt;
-        s.counters = cnt;
-    }
+    // Default capacities: 128-column partials on every SM, 64K tiles, 64 tokens x 32K digits.
+    int st;
+    if ((st = grow(&s.ws, &s.ws_floats, need.ws, (size_t)2 * num_sms * 128 * 128, stream, false, "partials")) ||
+        (st = grow(&s.counter_ptr, &s.counters, need.counters, (size_t)1 << 16, stream, true, "counters")) ||
+        (st = grow(&s.dig, &s.dig_bytes, need.dig, (size_t)4 * 64 * 32768, stream, false, "digits")) ||
+        (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)64, stream, false, "exponents")))
+        return st;
     *out = s;
     return B200Q8_OK;
 }
@@ -164,7 +169,8 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
                 const float* scales, const float* bias, const void* residual, size_t M, size_t N,
                 size_t K, cudaStream_t stream, int algo = B200Q8_ALGO_AUTO)
 {
-    if (algo != B200Q8_ALGO_AUTO && algo != B200Q8_ALGO_SIMT && algo != B200Q8_ALGO_TC)
+    if (algo != B200Q8_ALGO_AUTO && algo != B200Q8_ALGO_SIMT && algo != B200Q8_ALGO_TC &&
+        algo != B200Q8_ALGO_TC_I8)
         return fail(B200Q8_ERR_INVALID, "linear_q8: unknown algo %d", algo);
     if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
         return fail(B200Q8_ERR_INVALID, "linear_q8: dtype must be B200Q8_F32 or B200Q8_F16");
@@ -199,17 +205,49 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     a.out_dtype = out_dtype;
     a.pdl = true;
     cudaError_t e;
-    // fp16 activations: the tensor-core kernel for every M; fp32 activations: the SIMT GEMV.
+    // Kernel choice (AUTO): up to 16 tokens -> int8 tensor-core GEMV with exact activation digits;
+    // more tokens with fp16 activations -> fp16 tensor-core GEMM (weights dequantized into TMEM);
+    // more tokens with fp32 activations -> the digit kernel in groups of up to 64 tokens.
+    // Shapes the tensor-core kernels cannot take (K % 16 != 0, misaligned) use the SIMT GEMV.
     const bool tc_ok = gemm_tc_supports(a);
+    LinearArgs a1 = a;
+    a1.M = M < (size_t)gemv_i8_max_tokens() ? M : (size_t)gemv_i8_max_tokens();
+    const bool i8_ok = gemv_i8_supports(a1);
     if (algo == B200Q8_ALGO_TC && !tc_ok)
         return fail(B200Q8_ERR_UNSUPPORTED,
-                    "linear_q8: tensor-core path needs fp16 activations, K %% 16 == 0 and 16-byte aligned "
+                    "linear_q8: fp16 tensor-core path needs fp16 activations, K %% 16 == 0 and 16-byte aligned "
                     "weight/activation pointers (in_dtype=%d K=%zu)", in_dtype, K);
-    if (tc_ok && algo != B200Q8_ALGO_SIMT) {
+    if (algo == B200Q8_ALGO_TC_I8 && !i8_ok)
+        return fail(B200Q8_ERR_UNSUPPORTED,
+                    "linear_q8: int8 tensor-core path needs K %% 16 == 0, K <= 131072 and a 16-byte aligned "
+                    "weight pointer (K=%zu)", K);
+    const bool use_i8 = algo == B200Q8_ALGO_TC_I8 ||
+                        (algo == B200Q8_ALGO_AUTO && i8_ok && (M <= 16 || !tc_ok));
+    const bool use_tc = !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok));
+    if (use_tc) {
+        ScratchNeed need;
+        gemm_tc_scratch_need(a, d.num_sms, &need.ws, &need.counters);
         TcScratch scratch;
-        if ((st = get_scratch(a, d.num_sms, stream, &scratch))) return st;
+        if ((st = get_scratch(need, d.num_sms, stream, &scratch))) return st;
         e = launch_q8_gemm_tc(a, d.num_sms, scratch, stream);
         if (e != cudaSuccess) return cuda_fail(e, "q8_gemm_tc launch");
+        return B200Q8_OK;
+    }
+    if (use_i8) {
+        const size_t mt = (size_t)gemv_i8_max_tokens();
+        for (size_t m0 = 0; m0 < M; m0 += mt) {
+            LinearArgs b = a;
+            b.M = (M - m0 < mt) ? (M - m0) : mt;
+            b.x = (const char*)inp + m0 * K * ib;
+            b.out = (char*)out + m0 * N * ob;
+            b.res = residual ? (const char*)residual + m0 * N * ob : nullptr;
+            ScratchNeed need;
+            gemv_i8_scratch_need(b, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+            TcScratch scratch;
+            if ((st = get_scratch(need, d.num_sms, stream, &scratch))) return st;
+            e = launch_q8_gemv_i8(b, d.num_sms, scratch, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "q8_gemv_i8 launch");
+        }
         return B200Q8_OK;
     }
     if ((int)M <= gemv_max_tokens()) {
@@ -290,8 +328,11 @@ int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, int in_dtype,
 int b200q8_kernel_error(int* code, int clear)
 {
     if (!code) return fail(B200Q8_ERR_INVALID, "kernel_error: null code");
-    cudaError_t e = read_kernel_error(code, clear != 0);
+    int c1 = 0, c2 = 0;
+    cudaError_t e = read_kernel_error(&c1, clear != 0);
+    if (e == cudaSuccess) e = read_kernel_error_i8(&c2, clear != 0);
     if (e != cudaSuccess) return cuda_fail(e, "kernel_error: read device word");
+    *code = c1 | c2;
     if (clear && *code) {
         int dev = 0;
         if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");

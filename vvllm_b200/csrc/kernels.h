@@ -35,11 +35,24 @@ cudaError_t launch_q8_quantize(const float* w, size_t N, size_t K, int8_t* q, fl
 // tiles and per-tile arrival counters (zero between launches; every launch
 // leaves them zero unless a bounded wait gave up).
 struct TcScratch {
-    float* ws = nullptr;
+    float* ws = nullptr;         // partial accumulators (fp32 or int32 words)
     size_t ws_floats = 0;
-    int* counter_ptr = nullptr;
+    int* counter_ptr = nullptr;  // per-tile arrival counters
     size_t counters = 0;
+    int8_t* dig = nullptr;       // activation digits [4M, K] (int8 digit GEMV)
+    size_t dig_bytes = 0;
+    int* exps = nullptr;         // per-token exponents [M]
+    size_t exps_count = 0;
 };
+
+// Tensor-core GEMV for M <= gemv_i8_max_tokens() with exact 4-digit int8
+// activations (fp16 or fp32 inputs) and kind::i8 MMAs on the raw int8 weights.
+cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream);
+bool gemv_i8_supports(const LinearArgs& a);
+int gemv_i8_max_tokens();
+void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* dig_bytes,
+                          size_t* exps);
+cudaError_t read_kernel_error_i8(int* code, bool clear);
 
 // tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (decode, skinny and prefill).
 // Returns cudaErrorNotSupported when the shape is outside what it takes and

@@ -158,14 +158,31 @@ struct Ring {
     }
 };
 
+// Epilogue of up to 16 consecutive tokens of one output channel: element i goes to
+// o[i * ld]; v = acc * scale (+ bias) (+ res), in the reference's order.
 template <typename OT>
-__device__ __forceinline__ void epi_store(const SkParams& p, int m, int n, float acc, float scale, float bias)
+__device__ __forceinline__ void epi_chunk(OT* o, const OT* res, int ld, int cnt, const uint32_t (&d)[16], float scale,
+                                          float bias, bool has_bias)
 {
-    const long long o = (long long)m * p.N + n;
-    float v = __fmul_rn(acc, scale);
-    if (p.bias) v = __fadd_rn(v, bias);
-    if (p.res) v = __fadd_rn(v, load_as_f32<OT>(reinterpret_cast<const OT*>(p.res) + o));
-    store_out<OT>(reinterpret_cast<OT*>(p.out) + o, v);
+    if (cnt == 16) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            float v = __fmul_rn(__uint_as_float(d[i]), scale);
+            if (has_bias) v = __fadd_rn(v, bias);
+            if (res) v = __fadd_rn(v, load_as_f32<OT>(res + (size_t)i * ld));
+            store_out<OT>(o + (size_t)i * ld, v);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (i < cnt) {
+                float v = __fmul_rn(__uint_as_float(d[i]), scale);
+                if (has_bias) v = __fadd_rn(v, bias);
+                if (res) v = __fadd_rn(v, load_as_f32<OT>(res + (size_t)i * ld));
+                store_out<OT>(o + (size_t)i * ld, v);
+            }
+        }
+    }
 }
 
 template <int BN, int BK, int S, int SA, typename OT>
@@ -395,24 +412,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
             const bool whole = (k0 == 0 && k1 == p.kbpt);
             const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
-            float* wslot = p.ws + (size_t)slot * BN * kTileRows;
+            // workspace slot layout: [128 rows][BN tokens] fp32, so a row's partials are contiguous
+            float* wrow = p.ws + ((size_t)slot * kTileRows + r) * BN;
+            OT* orow = reinterpret_cast<OT*>(p.out) + (size_t)m0 * p.N + n;
+            const OT* rrow = p.res ? reinterpret_cast<const OT*>(p.res) + (size_t)m0 * p.N + n : nullptr;
 #pragma unroll 1
             for (int c0 = 0; c0 < mvalid; c0 += 16) {
                 uint32_t d[16];
                 __syncwarp();
                 tc::tmem_ld_32x32b_x16(d_tmem + c0, d);
                 tc::tmem_ld_wait();
+                if (whole) {
+                    if (nv) epi_chunk<OT>(orow + (size_t)c0 * p.N, rrow ? rrow + (size_t)c0 * p.N : nullptr, p.N,
+                                          min(16, mvalid - c0), d, scale, bias, p.bias != nullptr);
+                } else {
+                    float4* w4 = reinterpret_cast<float4*>(wrow + c0);
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const int mi = c0 + i;
-                    if (mi < mvalid) {
-                        const float a = __uint_as_float(d[i]);
-                        if (whole) {
-                            if (nv) epi_store<OT>(p, m0 + mi, n, a, scale, bias);
-                        } else {
-                            __stcg(wslot + mi * kTileRows + r, a);
-                        }
-                    }
+                    for (int i = 0; i < 4; i++)
+                        __stcg(w4 + i, make_float4(__uint_as_float(d[4 * i]), __uint_as_float(d[4 * i + 1]),
+                                                   __uint_as_float(d[4 * i + 2]), __uint_as_float(d[4 * i + 3])));
                 }
             }
             // accumulator drained: the MMA may reuse it
@@ -433,13 +451,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (*last_flag) {
                     __threadfence();
-                    for (int mi = 0; mi < mvalid; mi++) {
-                        float a = 0.0f;
-                        for (int j = j0; j <= j1; j++) {
-                            const int sj = (unit_begin(j, p.units, G) >= tb) ? 2 * j : 2 * j + 1;
-                            a += __ldcg(p.ws + ((size_t)sj * BN + mi) * kTileRows + r);
+#pragma unroll 1
+                    for (int c0 = 0; c0 < mvalid; c0 += 16) {
+                        float acc[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+#pragma unroll 1
+                        for (int j = j0; j <= j1; j += 2) {
+                            // two pieces in flight; summed in piece (= K) order
+                            const int sa_ = (unit_begin(j, p.units, G) >= tb) ? 2 * j : 2 * j + 1;
+                            const float4* pa = reinterpret_cast<const float4*>(
+                                p.ws + ((size_t)sa_ * kTileRows + r) * BN + c0);
+                            float4 va[4], vb[4];
+#pragma unroll
+                            for (int i = 0; i < 4; i++) va[i] = __ldcg(pa + i);
+                            const bool two = j + 1 <= j1;
+                            if (two) {
+                                const int sb_ = (unit_begin(j + 1, p.units, G) >= tb) ? 2 * (j + 1) : 2 * (j + 1) + 1;
+                                const float4* pb = reinterpret_cast<const float4*>(
+                                    p.ws + ((size_t)sb_ * kTileRows + r) * BN + c0);
+#pragma unroll
+                                for (int i = 0; i < 4; i++) vb[i] = __ldcg(pb + i);
+                            }
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                acc[4 * i] += va[i].x;
+                                acc[4 * i + 1] += va[i].y;
+                                acc[4 * i + 2] += va[i].z;
+                                acc[4 * i + 3] += va[i].w;
+                            }
+                            if (two) {
+#pragma unroll
+                                for (int i = 0; i < 4; i++) {
+                                    acc[4 * i] += vb[i].x;
+                                    acc[4 * i + 1] += vb[i].y;
+                                    acc[4 * i + 2] += vb[i].z;
+                                    acc[4 * i + 3] += vb[i].w;
+                                }
+                            }
                         }
-                        if (nv) epi_store<OT>(p, m0 + mi, n, a, scale, bias);
+                        uint32_t d[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) d[i] = __float_as_uint(acc[i]);
+                        if (nv)
+                            epi_chunk<OT>(orow + (size_t)c0 * p.N, rrow ? rrow + (size_t)c0 * p.N : nullptr, p.N,
+                                          min(16, mvalid - c0), d, scale, bias, p.bias != nullptr);
                     }
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                     if (etid == 0) p.counters[t] = 0;  // ready for the next launch

@@ -1,0 +1,658 @@
+// q8_gemv_tc.cu -- int8-weight GEMV / skinny GEMM on the tensor cores with exact
+// multi-digit activations (kind::i8), for M = 1..42 tokens per launch group.
+//
+// out[m, n] = (sum_k x[m, k] * float(W[n, k])) * scales[n] + bias[n] (+ res[m, n])
+// (semantics of vvllm BackendCPU::linear_q8 / linear_q8_add,
+//  src/backend/backend_naive.cc:155-291 and :322-335.)
+//
+// Decode streams every weight byte once, so the kernel must turn HBM bytes
+// into MACs with as little per-byte work as possible.  The int8 weights are
+// never converted: the TMA-loaded weight tile IS the MMA's A operand.  The
+// activations are made exact integers instead: x_q = x * 2^e with
+//   fp16 x: e = 24, which makes every finite fp16 value an integer below 2^40
+//           (exact, no data-dependent scale);
+//   fp32 x: e = 39 - floor(log2(max_k |x_m,k|)) per token (rounded to an
+//           integer, 2^-40 relative to the row maximum).
+// x_q is split into six base-128 digits (five unsigned 7-bit digits and a
+// signed top digit, all int8), which become 6*M rows of the MMA's B operand
+// (N = 6M padded to a multiple of 16; M = 1 decode pads to 16 anyway, so the
+// digits cost nothing).  tcgen05.mma.kind::i8 (K = 32 per instruction)
+// accumulates exact int32 digit sums in TMEM; the epilogue recombines them in
+// double (sum_d D_d * 2^(7d) * 2^-e), rounds once to fp32 and applies the
+// per-row scale, bias and residual in the reference's order.
+//
+// Pipeline (one CTA per SM, persistent stream-K over (128-row tile, K-stage)
+// units, exact int64 fixup of split tiles):
+//   warp 0     TMA producer: weight boxes [128 rows x 128 B], 128-byte swizzled,
+//              into an S-stage ring (starts at launch: weights never wait for
+//              the previous kernel);
+//   warp 1     TMEM allocator + one thread issuing BK/32 kind::i8 MMAs per stage;
+//   warps 2-5  epilogue: tcgen05.ld, digit recombination, stores / fixup;
+//   warps 6-9  digitizers: read x for the stage (after the prep kernel's
+//              per-token exponents are ready), write the six digit rows per
+//              token straight into the stage's swizzled B tile in shared memory.
+// A prep kernel (one CTA per token) computes the exponents and flags rows with
+// Inf/NaN (their outputs are NaN).  Every mbarrier wait is bounded; a timeout
+// sets a device error word, drains in-flight copies and MMAs, frees TMEM and
+// returns.  No TMA multicast and no clusters.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <limits.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sk_common.cuh"
+#include "tc_utils.cuh"
+
+namespace b200q8 {
+
+__device__ int g_kernel_error_i8;  // bit 0: a bounded wait timed out in the digit GEMV
+
+namespace {
+
+constexpr int kTileRows = 128;
+constexpr int kWarps = 10;
+constexpr int kThreads = kWarps * 32;
+constexpr int kFirstEpi = 2, kFirstDig = 6;
+constexpr int kDigits = 6;
+constexpr int kF16Exp = 24;  // 2^24 * fp16 is an integer for every finite fp16
+constexpr int kQBits = 40;   // |x_q| < 2^40
+constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
+constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
+
+struct DigParams {
+    const void* x;    // [M, K] fp16 or fp32
+    const float* scales;
+    const float* bias;
+    const void* res;
+    void* out;
+    const int* exps;  // [M] exponent per token (INT_MIN: the row holds Inf/NaN)
+    int* ws;          // [2 * gridDim.x][128][NC] int32 partial digit sums
+    int* counters;    // [tiles] arrival counters, zero between launches
+    int M, N, K;
+    int kbpt;
+    long long units;
+};
+
+template <int NC, int BK, int S>
+struct DigCfg {
+    static constexpr int kBoxes = BK / 128;  // 128-byte K boxes per stage
+    static constexpr int kWBytes = kTileRows * BK;
+    static constexpr int kDBoxBytes = NC * 128;
+    static constexpr int kDBytes = kBoxes * kDBoxBytes;
+    static constexpr int kDCols = (NC + 31) / 32 * 32;
+    static constexpr int kColsNeeded = 2 * kDCols;
+    static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
+                                     : kColsNeeded <= 256 ? 256 : 512;
+    static constexpr int kNumBars = 3 * S + 4 + 1;  // full, dfull, empty per stage; acc x4; drain
+    static constexpr int kSmemBytes = 1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16;
+    static_assert(NC % 16 == 0 && NC >= 16 && NC <= 256, "kind::i8 N for M=128");
+    static_assert(BK % 128 == 0, "whole 128-byte boxes");
+    static_assert(kColsNeeded <= 512, "TMEM overflow");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kDBoxBytes % 1024 == 0, "digit boxes stay 1024-byte aligned");
+};
+
+__device__ __forceinline__ void raise_error(volatile int* abort)
+{
+    *abort = 1;
+    atomicOr(&g_kernel_error_i8, 1);
+}
+
+// ----------------------------------------------------------------------------- prep
+// One CTA per token: the exponent e (fp16: 24; fp32: 39 - floor(log2(max|x|))) or
+// INT_MIN when the row holds Inf/NaN.
+template <typename XT>
+__global__ void __launch_bounds__(1024) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps)
+{
+    pdl_launch_dependents();  // the GEMV may start streaming weights right away
+    pdl_wait();               // x is written by the previous kernel
+    __shared__ float red[32];
+    __shared__ int bad_any;
+    const int m = blockIdx.x;
+    if (threadIdx.x == 0) bad_any = 0;
+    __syncthreads();
+    float mx = 0.0f;
+    int bad = 0;
+    if (sizeof(XT) == 2) {
+        const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x) + (size_t)m * K);
+        for (int i = threadIdx.x; i < (K >> 3); i += blockDim.x) {
+            const uint4 v = xr[i];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++)  // exponent field all ones: Inf or NaN
+                if (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) bad = 1;
+        }
+    } else {
+        const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + (size_t)m * K);
+        for (int i = threadIdx.x; i < (K >> 2); i += blockDim.x) {
+            const float4 v = xr[i];
+            const float a[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (a[j] <= FLT_MAX) mx = fmaxf(mx, a[j]); else bad = 1;  // NaN and Inf fail a <= FLT_MAX
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    if (bad) atomicOr(&bad_any, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m_all = 0.0f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) m_all = fmaxf(m_all, red[i]);
+        int e;
+        if (bad_any) e = INT_MIN;
+        else if (sizeof(XT) == 2) e = kF16Exp;
+        else e = (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
+        exps[m] = e;
+    }
+}
+
+// Six base-128 digits of q (|q| < 2^40): d0..d4 unsigned 7-bit, d5 signed.
+__device__ __forceinline__ void digits6(long long q, uint32_t (&d)[kDigits], int byte)
+{
+#pragma unroll
+    for (int i = 0; i < kDigits - 1; i++) d[i] |= (uint32_t)((q >> (7 * i)) & 127) << (8 * byte);
+    d[kDigits - 1] |= (uint32_t)((int)(q >> 35) & 0xFF) << (8 * byte);
+}
+
+__device__ __forceinline__ float recombine(const long long (&dsum)[kDigits], int e)
+{
+    if (e == INT_MIN) return __int_as_float(0x7fc00000);  // the token row holds Inf/NaN
+    double acc = 0.0;
+#pragma unroll
+    for (int i = kDigits - 1; i >= 0; i--) acc = acc * 128.0 + (double)dsum[i];
+    return __double2float_rn(ldexp(acc, -e));
+}
+
+template <typename OT>
+__device__ __forceinline__ void epi_one(OT* o, const OT* res, float acc, float scale, float bias, bool has_bias)
+{
+    float v = __fmul_rn(acc, scale);
+    if (has_bias) v = __fadd_rn(v, bias);
+    if (res) v = __fadd_rn(v, load_as_f32<OT>(res));
+    sk::store_out<OT>(o, v);
+}
+
+// ----------------------------------------------------------------------------- GEMV
+template <int NC, int BK, int S, typename XT, typename OT>
+__global__ void __launch_bounds__(kThreads, 1)
+    q8_gemv_dig_kernel(const __grid_constant__ CUtensorMap tmW, const DigParams p)
+{
+    using C = DigCfg<NC, BK, S>;
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~static_cast<uintptr_t>(1023));
+    unsigned char* sW = smem;
+    unsigned char* sD = smem + S * C::kWBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sD + S * C::kDBytes);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+
+    const uint32_t bar0 = tc::smem_u32(bars);
+    const uint32_t full0 = bar0, dfull0 = bar0 + 8u * S, empty0 = bar0 + 16u * S, accfull0 = bar0 + 24u * S,
+                   accempty0 = accfull0 + 16u, drainbar = accfull0 + 32u;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const int cta = blockIdx.x;
+    const long long u_begin = sk::unit_begin(cta, p.units, G), u_end = sk::unit_begin(cta + 1, p.units, G);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            tc::mbar_init(full0 + 8u * s, 1);
+            tc::mbar_init(dfull0 + 8u * s, 4);
+            tc::mbar_init(empty0 + 8u * s, 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(accfull0 + 8u * b, 1);
+            tc::mbar_init(accempty0 + 8u * b, 4);
+        }
+        tc::mbar_init(drainbar, 1);
+        *abort = 0;
+        tc::fence_mbar_init();
+    }
+    if (threadIdx.x == 32) tc::prefetch_tensormap(&tmW);
+    // Digit rows past 6M stay zero for the whole kernel: clear every stage's B tile once.
+    for (int i = threadIdx.x; i < S * C::kDBytes / 16; i += kThreads)
+        reinterpret_cast<uint4*>(sD)[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
+    __syncwarp();
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_holder), C::kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (weights)
+        if (lane == 0) {
+            sk::Ring st;
+            int issued = 0;
+            bool ok = true;
+            int t, k0, k1;
+            sk::SegIter it(u_begin, u_end, p.kbpt);
+            const uint32_t sw_base = tc::smem_u32(sW);
+            while (ok && it.next(t, k0, k1)) {
+                const int row0 = t * kTileRows;
+                for (int kb = k0; kb < k1; kb++) {
+                    if (issued >= S &&
+                        !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
+                        raise_error(abort);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full0 + 8u * st.idx;
+                    tc::mbar_arrive_expect_tx(fb, C::kWBytes);
+#pragma unroll
+                    for (int h = 0; h < C::kBoxes; h++)
+                        tc::tma_load_2d(sw_base + st.idx * C::kWBytes + h * (kTileRows * 128), &tmW, kb * BK + h * 128,
+                                        row0, fb);
+                    issued++;
+                    st.next(S);
+                }
+            }
+            if (*abort) {
+                const int zero = 0;
+                sk::Ring d;
+                for (int q = 0; q < issued; q++, d.next(S))
+                    if (q + S >= issued) tc::mbar_wait(full0 + 8u * d.idx, d.phase, &zero, kWaitTimeoutNs);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::make_idesc_s8_s32(kTileRows, NC);
+            sk::Ring st;
+            int seg = 0, t, k0, k1;
+            sk::SegIter it(u_begin, u_end, p.kbpt);
+            bool ok = true;
+            const uint64_t adesc0 = tc::make_sw128_kmajor_desc(tc::smem_u32(sW));
+            const uint64_t bdesc0 = tc::make_sw128_kmajor_desc(tc::smem_u32(sD));
+            while (ok && it.next(t, k0, k1)) {
+                const int ab = seg & 1, use = seg >> 1;
+                if (use > 0 &&
+                    !tc::mbar_wait(accempty0 + 8u * ab, (uint32_t)((use - 1) & 1), abort, kWaitTimeoutNs)) {
+                    raise_error(abort);
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d_tmem = tmem + ab * C::kDCols;
+                for (int kb = k0; kb < k1; kb++) {
+                    if (!tc::mbar_wait(full0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs) ||
+                        !tc::mbar_wait(dfull0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs)) {
+                        raise_error(abort);
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint64_t a_stage = adesc0 + (uint64_t)((st.idx * C::kWBytes) >> 4);
+                    const uint64_t b_stage = bdesc0 + (uint64_t)((st.idx * C::kDBytes) >> 4);
+#pragma unroll
+                    for (int j = 0; j < BK / 32; j++)
+                        tc::mma_s8_ss(d_tmem, a_stage + (uint64_t)(((j >> 2) * (kTileRows * 128) + (j & 3) * 32) >> 4),
+                                      b_stage + (uint64_t)(((j >> 2) * C::kDBoxBytes + (j & 3) * 32) >> 4), idesc,
+                                      (kb != k0 || j != 0) ? 1u : 0u);
+                    tc::mma_commit(empty0 + 8u * st.idx);
+                    st.next(S);
+                }
+                if (!ok) break;
+                tc::mma_commit(accfull0 + 8u * ab);
+                seg++;
+            }
+            if (*abort) {
+                const int zero = 0;
+                tc::mma_commit(drainbar);
+                tc::mbar_wait(drainbar, 0, &zero, kWaitTimeoutNs);
+            }
+        }
+    } else if (warp >= kFirstDig) {
+        // ------------------------------------------------------------ digitizers
+        const int dtid = threadIdx.x - kFirstDig * 32;  // 0..127
+        pdl_wait();  // x and the prep kernel's exponents are ready
+        sk::Ring st;
+        int g = 0, t, k0, k1;
+        sk::SegIter it(u_begin, u_end, p.kbpt);
+        bool ok = true;
+        const XT* xg = reinterpret_cast<const XT*>(p.x);
+        while (ok && it.next(t, k0, k1)) {
+            for (int kb = k0; kb < k1; kb++, g++, st.next(S)) {
+                if (g >= S) {
+                    ok = __all_sync(0xffffffffu,
+                                    tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs));
+                    if (!ok) break;
+                }
+                unsigned char* bst = sD + st.idx * C::kDBytes;
+                // thread -> 4 consecutive k of one token; BK/4 groups per token per stage
+                for (int item = dtid; item < p.M * (BK / 4); item += 128) {
+                    const int m = item / (BK / 4);
+                    const int kk = (item - m * (BK / 4)) * 4;  // 0..BK-4
+                    const int k = kb * BK + kk;
+                    const int e = p.exps[m];
+                    uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
+                    if (k < p.K && e != INT_MIN) {
+                        float v[4];
+                        if (sizeof(XT) == 2) {
+                            const uint2 raw = *reinterpret_cast<const uint2*>(xg + (size_t)m * p.K + k);
+                            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                            v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+                        } else {
+                            const float4 raw = *reinterpret_cast<const float4*>(xg + (size_t)m * p.K + k);
+                            v[0] = raw.x; v[1] = raw.y; v[2] = raw.z; v[3] = raw.w;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
+                    }
+                    const int h = kk >> 7, c = (kk & 127) >> 4, byte = kk & 15;
+#pragma unroll
+                    for (int i = 0; i < kDigits; i++) {
+                        const int r = m * kDigits + i;
+                        *reinterpret_cast<uint32_t*>(bst + h * C::kDBoxBytes + r * 128 + ((c ^ (r & 7)) << 4) + byte) =
+                            d[i];
+                    }
+                }
+                // generic-proxy writes -> visible to the tensor core's async-proxy reads
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(dfull0 + 8u * st.idx);
+            }
+        }
+        if (!ok) raise_error(abort);
+    } else {
+        // ------------------------------------------------------------ epilogue
+        pdl_wait();  // exps come from the prep kernel
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+        const int etid = threadIdx.x - kFirstEpi * 32;
+        const bool has_bias = p.bias != nullptr;
+        int seg = 0, t, k0, k1;
+        sk::SegIter it(u_begin, u_end, p.kbpt);
+        bool ok = true;
+        OT* out = reinterpret_cast<OT*>(p.out);
+        const OT* res = reinterpret_cast<const OT*>(p.res);
+        const int ncols = kDigits * p.M;
+        while (it.next(t, k0, k1)) {
+            const int ab = seg & 1, use = seg >> 1;
+            ok = __all_sync(0xffffffffu,
+                            tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            if (!ok) break;
+            tc::tc_fence_after();
+            const int n = t * kTileRows + r;
+            const bool nv = n < p.N;
+            const float scale = nv ? p.scales[n] : 0.0f;
+            const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
+            const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
+            const bool whole = (k0 == 0 && k1 == p.kbpt);
+            const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
+            int* wrow = p.ws + ((size_t)slot * kTileRows + r) * NC;
+            // Each token's six digit sums sit in consecutive TMEM columns; take 8 tokens
+            // (48 columns, three 16-column loads) at a time.
+#pragma unroll 1
+            for (int mg = 0; mg < p.M; mg += 8) {
+                const int base = mg * kDigits;
+                int dreg[48];
+#pragma unroll
+                for (int c = 0; c < 48; c += 16) {
+                    if (base + c < ncols) {
+                        uint32_t d[16];
+                        __syncwarp();
+                        tc::tmem_ld_32x32b_x16(d_tmem + base + c, d);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) dreg[c + i] = (int)d[i];
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i++) dreg[c + i] = 0;
+                    }
+                }
+                if (whole) {
+                    if (nv) {
+#pragma unroll
+                        for (int tt = 0; tt < 8; tt++) {
+                            const int m = mg + tt;
+                            if (m < p.M) {
+                                long long ds[kDigits];
+#pragma unroll
+                                for (int i = 0; i < kDigits; i++) ds[i] = dreg[tt * kDigits + i];
+                                const size_t o = (size_t)m * p.N + n;
+                                epi_one<OT>(out + o, res ? res + o : nullptr, recombine(ds, p.exps[m]), scale, bias,
+                                            has_bias);
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 48; c += 4)
+                        if (base + c < ncols)
+                            __stcg(reinterpret_cast<int4*>(wrow + base + c),
+                                   make_int4(dreg[c], dreg[c + 1], dreg[c + 2], dreg[c + 3]));
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(accempty0 + 8u * ab);  // accumulator drained
+            if (!whole) {
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                const long long tb = (long long)t * p.kbpt;
+                const int j0 = sk::cta_of_unit(tb, p.units, G);
+                const int j1 = sk::cta_of_unit(tb + p.kbpt - 1, p.units, G);
+                if (etid == 0) {
+                    const int prev = atomicAdd(p.counters + t, 1);
+                    *last_flag = (prev == j1 - j0) ? 1 : 0;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (*last_flag) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int m = 0; m < p.M; m++) {
+                        long long ds[kDigits] = {0, 0, 0, 0, 0, 0};
+#pragma unroll 1
+                        for (int j = j0; j <= j1; j++) {
+                            const int* pj = p.ws + ((size_t)sk::piece_slot(j, tb, p.units, G) * kTileRows + r) * NC +
+                                            m * kDigits;
+#pragma unroll
+                            for (int i = 0; i < kDigits; i++) ds[i] += __ldcg(pj + i);
+                        }
+                        if (nv) {
+                            const size_t o = (size_t)m * p.N + n;
+                            epi_one<OT>(out + o, res ? res + o : nullptr, recombine(ds, p.exps[m]), scale, bias,
+                                        has_bias);
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (etid == 0) p.counters[t] = 0;
+                }
+            }
+            seg++;
+        }
+        if (!ok) raise_error(abort);
+        pdl_launch_dependents();
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// ----------------------------------------------------------------------------- host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// int8 [rows, K] row-major in [box_rows x 128 B] boxes, 128-byte swizzle, out-of-range reads 0.
+bool make_i8_map(CUtensorMap* m, const void* base, size_t K, size_t rows, int box_rows)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint32_t es[2] = {1, 1};
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int pick_nc(size_t M)
+{
+    const int need = (int)(kDigits * M);
+    return need <= 16 ? 16 : need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : 256;
+}
+int pick_bk_i8(int NC) { return NC <= 16 ? 512 : NC <= 64 ? 256 : 128; }
+
+template <typename Kern, typename... Args>
+cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    if (e == cudaSuccess) note_launch();
+    return e;
+}
+
+template <int NC, int BK, int S, typename XT, typename OT>
+cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cudaStream_t stream)
+{
+    using C = DigCfg<NC, BK, S>;
+    CUtensorMap mw;
+    if (!make_i8_map(&mw, a.w, a.K, a.N, kTileRows)) return cudaErrorInvalidValue;
+    auto kern = q8_gemv_dig_kernel<NC, BK, S, XT, OT>;
+    static thread_local bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    DigParams p;
+    p.x = a.x;
+    p.scales = a.scales;
+    p.bias = a.bias;
+    p.res = a.res;
+    p.out = a.out;
+    p.exps = sc.exps;
+    p.ws = reinterpret_cast<int*>(sc.ws);
+    p.counters = sc.counter_ptr;
+    p.M = (int)a.M;
+    p.N = (int)a.N;
+    p.K = (int)a.K;
+    p.kbpt = (int)((a.K + BK - 1) / BK);
+    const long long tiles = (long long)((a.N + kTileRows - 1) / kTileRows);
+    p.units = tiles * p.kbpt;
+    const int G = (int)((p.units < num_sms) ? p.units : num_sms);
+    if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
+        sc.exps_count < a.M)
+        return cudaErrorMemoryAllocation;
+    e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M), dim3(1024), 0, stream, a.pdl,
+                  reinterpret_cast<const XT*>(a.x), (int)a.K, sc.exps);
+    if (e != cudaSuccess) return e;
+    return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
+}
+
+template <typename XT, typename OT>
+cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& sc, cudaStream_t stream)
+{
+    switch (pick_nc(a.M)) {
+        case 16: return launch_cfg<16, 512, 3, XT, OT>(a, num_sms, sc, stream);
+        case 32: return launch_cfg<32, 256, 5, XT, OT>(a, num_sms, sc, stream);
+        case 64: return launch_cfg<64, 256, 4, XT, OT>(a, num_sms, sc, stream);
+        case 128: return launch_cfg<128, 128, 6, XT, OT>(a, num_sms, sc, stream);
+        default: return launch_cfg<256, 128, 4, XT, OT>(a, num_sms, sc, stream);
+    }
+}
+
+}  // namespace
+
+int gemv_i8_max_tokens() { return kMaxTokens; }
+
+bool gemv_i8_supports(const LinearArgs& a)
+{
+    const size_t xa = a.in_dtype == kF16 ? 8 : 16;  // 4-element vector loads of x
+    return a.M >= 1 && a.M <= (size_t)kMaxTokens && a.K % 16 == 0 && a.K >= 16 && a.K <= 131072 &&
+           ((uintptr_t)a.w % 16) == 0 && ((uintptr_t)a.x % xa) == 0 && a.N >= 1 && a.N <= (size_t)INT32_MAX &&
+           encode_fn() != nullptr;
+}
+
+void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* dig_bytes,
+                          size_t* exps)
+{
+    const int NC = pick_nc(a.M);
+    const int BK = pick_bk_i8(NC);
+    const long long tiles = (long long)((a.N + kTileRows - 1) / kTileRows);
+    const long long units = tiles * (long long)((a.K + BK - 1) / BK);
+    const long long G = units < num_sms ? units : num_sms;
+    *ws_floats = (size_t)(2 * G * NC * kTileRows);
+    *counters = (size_t)tiles;
+    *dig_bytes = 0;
+    *exps = a.M;
+}
+
+cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& sc, cudaStream_t stream)
+{
+    if (!gemv_i8_supports(a)) return cudaErrorNotSupported;
+    if (a.in_dtype == kF16)
+        return a.out_dtype == kF16 ? launch_typed<__half, __half>(a, num_sms, sc, stream)
+                                   : launch_typed<__half, float>(a, num_sms, sc, stream);
+    return a.out_dtype == kF16 ? launch_typed<float, __half>(a, num_sms, sc, stream)
+                               : launch_typed<float, float>(a, num_sms, sc, stream);
+}
+
+cudaError_t read_kernel_error_i8(int* code, bool clear)
+{
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_kernel_error_i8, sizeof(int));
+    if (e != cudaSuccess) return e;
+    *code = v;
+    if (clear && v) {
+        const int z = 0;
+        e = cudaMemcpyToSymbol(g_kernel_error_i8, &z, sizeof(int));
+    }
+    return e;
+}
+
+}  // namespace b200q8

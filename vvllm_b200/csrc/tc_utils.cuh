@@ -141,6 +141,27 @@ __host__ __device__ constexpr uint32_t make_idesc_f16_f32(int M, int N)
            | ((uint32_t)(M >> 4) << 24);    // M / 16
 }
 
+// kind::i8 instruction descriptor: signed int8 A and B (K-major), int32 D.
+__host__ __device__ constexpr uint32_t make_idesc_s8_s32(int M, int N)
+{
+    return (2u << 4)                        // D format: s32
+           | (1u << 7) | (1u << 10)         // A, B format: signed 8-bit
+           | (0u << 15) | (0u << 16)        // A, B K-major
+           | ((uint32_t)(N >> 3) << 17)
+           | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T over K = 32 int8, one elected thread.
+__device__ __forceinline__ void mma_s8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate)
+{
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, one elected thread.
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate)
