@@ -223,7 +223,10 @@ def profile_case(args):
 
     name, _, m = args.profile_case.partition(":")
     M = int(m) if m else 1
-    N, K = {n: (N, K) for n, N, K in PROJ}[name]
+    if "x" in name:  # explicit N x K (e.g. "4864x896:512", a prefill GEMM of BASELINE config 4)
+        N, K = (int(v) for v in name.split("x"))
+    else:
+        N, K = {n: (N, K) for n, N, K in PROJ}[name]
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
@@ -409,7 +412,7 @@ def main():
                                   f"{cores} threads; CPU: {model}"}
 
     if rank == 0:
-        traffic = profiled_traffic("q8_gemv_lm_head")
+        traffic = profiled_traffic("q8_gemv_dig_lm_head_7b") if world == 1 else None
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
@@ -418,7 +421,7 @@ def main():
             "config": {"workload": WORKLOAD, "M": 1, "activations": "fp16", "parallelism": f"column-shard x{world}",
                        "collective": "NCCL allgather" if world > 1 else "none",
                        "l2": f"{copies} rotating weight set(s), {copies * per_rank_bytes / 1e6:.0f} MB per rank per cycle (> L2)"},
-            "roofline": {"bound": "hbm", "kernel": "q8_gemv (lm_head shard)", "achieved": round(lm_gbs, 2),
+            "roofline": {"bound": "hbm", "kernel": "q8_gemv_dig_kernel (lm_head shard)", "achieved": round(lm_gbs, 2),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(lm_gbs / hbm_peak, 4),
                          "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": round(lm_ms, 5)},
