@@ -102,6 +102,24 @@ B200Q8_API int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, in
                                    const void* residual, size_t M, size_t N, size_t K, int algo,
                                    b200q8_stream_t stream);
 
+/* Allocation-free linear_q8 / linear_q8_add (residual may be NULL), for
+ * callers that may not call cudaMalloc: a device-memory pool or budget they
+ * must not bypass, or a decode loop that cannot take the device-wide
+ * synchronisation cudaMalloc and cudaFree may cause.  No counterpart in the
+ * reference (vvllm has no allocation-free path).  It runs the int8 tensor-core
+ * GEMV with its scratch in a fixed device array of about 2.6 MB that every GPU
+ * loading this library holds until exit, and allocates nothing.  Limits: M <= 2
+ * tokens, N <= 524288 rows, K % 16 == 0 with 16 <= K <= 131072, at most 160 SMs;
+ * larger shapes return B200Q8_ERR_UNSUPPORTED.  The first call on a device looks
+ * up the array's device address; make that first call before any stream
+ * capture.  All calls share the array, which keeps the last call's contents
+ * (each call clears the counters it needs); calls that overlap on one GPU race
+ * on it and must be serialised by the caller. */
+B200Q8_API int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* inp, int in_dtype,
+                                        const int8_t* weight, const float* scales, const float* bias,
+                                        const void* residual, size_t M, size_t N, size_t K,
+                                        b200q8_stream_t stream);
+
 /* Device error word of the current device: bit 0 is set when a bounded wait
  * inside the tensor-core kernel gave up (its outputs are then invalid).
  * clear != 0 resets it.  Synchronises with the device. */

@@ -36,6 +36,7 @@ _SIGS = {
     "b200q8_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_linear_q8_ex": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _int, _vp], _int),
     "b200q8_kernel_error": ([ctypes.POINTER(_int), _int], _int),
+    "b200q8_linear_q8_noalloc": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_backend_create": ([_int, _int, ctypes.POINTER(_vp)], _int),
     "b200q8_backend_destroy": ([_vp], _int),
     "b200q8_backend_set_stream": ([_vp, _vp], _int),

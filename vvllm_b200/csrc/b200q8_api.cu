@@ -341,6 +341,61 @@ int b200q8_kernel_error(int* code, int clear)
     return B200Q8_OK;
 }
 
+// Allocation-free linear_q8 / linear_q8_add for callers that may not call
+// cudaMalloc (a device-memory pool or budget they must not bypass, or a decode
+// loop that cannot take cudaMalloc's device-wide synchronisation).  Runs the
+// int8 digit GEMV on the fixed device array of q8_gemv_tc.cu.
+int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
+                             const float* scales, const float* bias, const void* residual, size_t M, size_t N,
+                             size_t K, b200q8_stream_t stream)
+{
+    if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8_noalloc: dtype must be B200Q8_F32 or B200Q8_F16");
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!out || !inp || !weight || !scales)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_noalloc: null out/inp/weight/scales");
+    if (K == 0 || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX || N * K / K != N)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_noalloc: bad sizes (N=%zu K=%zu)", N, K);
+    const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4, ib = in_dtype == B200Q8_F16 ? 2 : 4;
+    {
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t i0 = (uintptr_t)inp, i1 = i0 + M * K * ib;
+        if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8_noalloc: inp overlaps out");
+        if (residual && residual != out) {
+            const uintptr_t r0 = (uintptr_t)residual, r1 = r0 + M * N * ob;
+            if (o0 < r1 && r0 < o1)
+                return fail(B200Q8_ERR_INVALID, "linear_q8_noalloc: residual partially overlaps out");
+        }
+    }
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+    LinearArgs a;
+    a.x = inp;
+    a.w = weight;
+    a.scales = scales;
+    a.bias = bias;
+    a.res = residual;
+    a.out = out;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.in_dtype = in_dtype;
+    a.out_dtype = out_dtype;
+    a.pdl = true;
+    cudaError_t e = cudaSuccess;
+    switch (launch_q8_gemv_i8_noalloc(a, d.num_sms, (cudaStream_t)stream, &e)) {
+        case 0: return B200Q8_OK;
+        case 1: return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_noalloc: M=%zu exceeds the fixed scratch (at most 2 tokens)", M);
+        case 2: return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_noalloc: N=%zu exceeds the fixed scratch (at most 524288 rows)", N);
+        case 3: return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_noalloc: %d SMs exceed the fixed scratch (at most 160)", d.num_sms);
+        case 4: return fail(B200Q8_ERR_UNSUPPORTED,
+                            "linear_q8_noalloc: needs K %% 16 == 0, 16 <= K <= 131072, a 16-byte aligned weight and an "
+                            "8-byte (fp16) / 16-byte (fp32) aligned input (K=%zu)", K);
+        default: return cuda_fail(e, "linear_q8_noalloc");
+    }
+}
+
 int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype,
                          const int8_t* weight, const float* scales, const float* bias,
                          const void* residual, size_t M, size_t N, size_t K, b200q8_stream_t stream)

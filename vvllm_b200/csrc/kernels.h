@@ -54,6 +54,11 @@ void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, s
                           size_t* exps);
 cudaError_t read_kernel_error_i8(int* code, bool clear);
 
+// The int8 digit GEMV on a fixed file-scope device array instead of allocated
+// scratch (see q8_gemv_tc.cu).  0: launched; 1..4: the shape exceeds the
+// array's limits (tokens, rows, SM count, K/alignment); -1: CUDA error in *err.
+int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t stream, cudaError_t* err);
+
 // tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (decode, skinny and prefill).
 // Returns cudaErrorNotSupported when the shape is outside what it takes and
 // cudaErrorMemoryAllocation when `scratch` is smaller than gemm_tc_scratch_need says.

@@ -655,4 +655,86 @@ cudaError_t read_kernel_error_i8(int* code, bool clear)
     return e;
 }
 
+// ============================================================================
+// Allocation-free variant of the int8 digit GEMV (b200q8_linear_q8_noalloc).
+//
+// Some callers may not call cudaMalloc: hosts whose device memory belongs to a
+// pool or budget that nothing may bypass (vvllm's own tensors come from a
+// caching pool, src/tensor/tensor.cc:35-68), and latency-critical decode loops
+// that cannot take the device-wide synchronisation cudaMalloc and cudaFree may
+// cause.  The regular entry points allocate their stream-K scratch lazily;
+// this one uses a fixed file-scope device array instead, so it allocates
+// nothing.  Every GPU that loads the library holds the array (kNoAllocBytes,
+// about 2.6 MB) until the process exits.  All calls share it and it keeps the
+// last call's contents; the tile counters, which must start at zero, are
+// cleared by every call.  Calls that overlap on one GPU (for example on two
+// streams) race on the array and must be serialised by the caller; each GPU
+// has its own copy.
+// ============================================================================
+namespace {
+
+constexpr int kNoAllocMaxTokens = 2;      // 6 digit rows per token: NC = 16
+constexpr int kNoAllocMaxCtas = 160;      // stream-K CTAs (a B200 has 148 SMs)
+constexpr int kNoAllocMaxTiles = 4096;    // 128-row tiles: N <= 524288
+constexpr size_t kNoAllocPartialInts = (size_t)2 * kNoAllocMaxCtas * kTileRows * 16;
+constexpr size_t kNoAllocExps = 64;
+constexpr size_t kNoAllocBytes = (kNoAllocPartialInts + kNoAllocMaxTiles + kNoAllocExps) * sizeof(int);
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[64];
+
+// Device address of the array on the current device, looked up once per device
+// (the first call on a device does this set-up).
+cudaError_t noalloc_base(int dev, void** out)
+{
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_base[dev] = p;
+    }
+    *out = g_noalloc_base[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+
+// Returns 0 and launches, or a reason the shape exceeds the array's limits
+// (1: tokens, 2: rows, 3: SM count, 4: K / alignment), or -1 with *err set.
+int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t stream, cudaError_t* err)
+{
+    *err = cudaSuccess;
+    if (a.M > (size_t)kNoAllocMaxTokens) return 1;
+    const size_t tiles = (a.N + kTileRows - 1) / kTileRows;
+    if (tiles > (size_t)kNoAllocMaxTiles) return 2;
+    if (num_sms > kNoAllocMaxCtas) return 3;
+    if (!gemv_i8_supports(a)) return 4;
+    int dev = 0;
+    if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return -1;
+    if (dev < 0 || dev >= 64) {
+        *err = cudaErrorInvalidDevice;
+        return -1;
+    }
+    void* base = nullptr;
+    if ((*err = noalloc_base(dev, &base)) != cudaSuccess) return -1;
+    TcScratch sc;
+    sc.ws = reinterpret_cast<float*>(base);
+    sc.ws_floats = kNoAllocPartialInts;
+    sc.counter_ptr = reinterpret_cast<int*>(base) + kNoAllocPartialInts;
+    sc.counters = kNoAllocMaxTiles;
+    sc.exps = sc.counter_ptr + kNoAllocMaxTiles;
+    sc.exps_count = kNoAllocExps;
+    // the counters must start at zero: clear the ones this call uses (no allocation)
+    if ((*err = cudaMemsetAsync(sc.counter_ptr, 0, tiles * sizeof(int), stream)) != cudaSuccess) return -1;
+    *err = launch_q8_gemv_i8(a, num_sms, sc, stream);
+    return *err == cudaSuccess ? 0 : -1;
+}
+
 }  // namespace b200q8
