@@ -214,6 +214,48 @@ def run_reference(args):
     return 0
 
 
+PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N), M = 512
+
+
+def prefill_tflops(v, dev, stream, warmup: int, iters: int, tc_peak: float):
+    """Config 4: four prefill GEMMs back to back; TFLOP/s of the whole set and per shape."""
+    import torch
+
+    M = 512
+    torch.manual_seed(1)
+    cases = []
+    for K, N in PREFILL:
+        q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+        s = torch.rand(N, device=dev) * 1e-3
+        x = torch.randn(M, K, device=dev).half()
+        out = torch.empty(M, N, device=dev, dtype=torch.float16)
+        cases.append((K, N, q, s, x, out))
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    per = {}
+    total_flop, total_ms = 0.0, 0.0
+    for K, N, q, s, x, out in cases:
+        for _ in range(warmup):
+            v.linear_q8(out, x, q, s, stream=stream)
+        ms = []
+        for _ in range(iters):
+            flush.zero_()  # the GEMM's operands come from HBM, not L2
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            v.linear_q8(out, x, q, s, stream=stream)
+            b.record(stream)
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        t = statistics.median(ms)
+        flop = 2.0 * M * N * K
+        per[f"{K}x{N}"] = {"TFLOP/s": round(flop / (t * 1e-3) / 1e12, 1), "us": round(t * 1e3, 2)}
+        total_flop += flop
+        total_ms += t
+    value = total_flop / (total_ms * 1e-3) / 1e12
+    return {"value": round(value, 1), "unit": "TFLOP/s", "frac": round(value / tc_peak, 4),
+            "peak": tc_peak, "M": M, "per_shape": per,
+            "timing": "median single launch per shape, L2 flushed before each, host launch cost included"}
+
+
 def profile_case(args):
     """Small single-projection run for ncu: warmup + 1 launches of one linear_q8 on one GPU.
     Weights are random int8 made with one torch launch (values do not change the memory traffic)."""
@@ -361,6 +403,25 @@ def main():
     lm_bytes = algo_bytes(lm_rows, HIDDEN)
     lm_gbs = lm_bytes / (lm_ms * 1e-3) / 1e9
 
+    # ---- N > 1: the same steps without the all-gathers (compute share of the step) ---------
+    compute_only = None
+    if comm is not None:
+        saved, comm = comm, None
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for it in range(args.steps):
+            step(it)
+        c1.record(stream)
+        barrier()
+        c_ms = c0.elapsed_time(c1)
+        t = torch.tensor([c_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        c_ms = t.item()
+        compute_only = {"value": round(total_bytes / (c_ms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+                        "ms_per_step": round(c_ms / args.steps, 5)}
+        comm = saved
+
     # ---- end to end through the C ABI with host buffers -------------------------------------
     h_in = [torch.empty((1, K), dtype=torch.float16).pin_memory() for (_, _, K, _, _, _, _) in shards]
     for h, x in zip(h_in, xs):
@@ -398,6 +459,11 @@ def main():
         e_ms = t.item()
     e2e_value = total_bytes / (e_ms / args.steps * 1e-3) / 1e9
 
+    # ---- prefill GEMM TFLOP/s (M = 512, fp16 in/out), rank 0 at N = 1 ------
+    prefill = None
+    if world == 1:
+        prefill = prefill_tflops(v, dev, stream, args.warmup, max(5, args.steps // 10), tc_peak)
+
     # ---- CPU baseline: the reference's linear_q8 on the host cores (rank 0, N = 1) ------------
     cpu_baseline = None
     if world == 1 and not args.no_cpu_baseline:
@@ -431,6 +497,10 @@ def main():
             "gpu_launches": int(n_launch),
             "clocks": sampler.summary(),
         }
+        if compute_only is not None:
+            line["compute_only"] = compute_only
+        if prefill is not None:
+            line["prefill"] = prefill
         if cpu_baseline is not None:
             line["cpu_baseline"] = cpu_baseline
         print(json.dumps(line), flush=True)

@@ -1,0 +1,99 @@
+"""Column-sharded linear_q8 over 2 GPUs with the library's NCCL all-gather (needs >= 2 GPUs).
+
+Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range), runs
+b200q8_linear_q8_sharded, and must end with the full [M, N] output.  Checked
+against the unsharded single-GPU result (the int8 digit GEMV sums exact
+integers, so sharding cannot change its result) and against the CPU oracle on
+a row sample.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from tests._util import TOL_F16, make_weight, make_x, rowwise_normwise_err, sample_rows
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # M, N, K
+    (1, 37888, 3584),   # 7B gate/up: direct in-place all-gather
+    (4, 1001, 896),     # ragged shards + rank-major permute
+    (1, 3584, 18944),   # 7B down: long K, split tiles on every rank
+    (8, 4736, 3584),    # several tokens
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, path):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import vvllm_b200 as v
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    uid = [v.Comm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    comm = v.Comm(rank, world, rank, uid[0], timeout_s=60.0)
+    results = {}
+    for ci, (M, N, K) in enumerate(CASES):
+        data = np.load(os.path.join(path, f"case{ci}.npz"))
+        q, s, x = data["q"], data["s"], data["x"]
+        r0, rows = v.shard_range(N, world, rank)
+        qt = torch.from_numpy(np.ascontiguousarray(q[r0:r0 + rows])).to(dev)
+        st = torch.from_numpy(s[r0:r0 + rows].copy()).to(dev)
+        xt = torch.from_numpy(x).to(dev).half()
+        per = -(-N // world)
+        out = torch.zeros((M, N), dtype=torch.float16, device=dev)
+        gather = None if (M == 1 and N % world == 0) else torch.zeros(world * M * per, dtype=torch.float16,
+                                                                          device=dev)
+        for _ in range(2):  # twice: the second call must not depend on leftovers of the first
+            v.linear_q8_sharded(comm, out, xt, qt, st, None, N, gather=gather)
+        torch.cuda.synchronize()
+        results[f"out{ci}"] = out.float().cpu().numpy()
+        if rank == 0:  # the unsharded result on one GPU
+            full = torch.empty((M, N), dtype=torch.float16, device=dev)
+            v.linear_q8(full, xt, torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev))
+            torch.cuda.synchronize()
+            results[f"full{ci}"] = full.float().cpu().numpy()
+    assert v.kernel_error() == 0
+    np.savez(os.path.join(path, f"rank{rank}.npz"), **results)
+    dist.barrier()
+    comm.destroy()
+    dist.destroy_process_group()
+
+
+def test_sharded_two_gpus(tmp_path, oracle):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    for ci, (M, N, K) in enumerate(CASES):
+        q, s = oracle.quantize_per_channel(make_weight(N, K, 900 + ci))
+        x = make_x(M, K, 910 + ci).astype(np.float16).astype(np.float32)
+        np.savez(tmp_path / f"case{ci}.npz", q=q, s=s, x=x)
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    r = [np.load(tmp_path / f"rank{i}.npz") for i in range(world)]
+    for ci, (M, N, K) in enumerate(CASES):
+        full = r[0][f"full{ci}"]
+        for i in range(world):
+            got = r[i][f"out{ci}"]
+            assert rowwise_normwise_err(got, full) <= TOL_F16, (ci, i)
+        data = np.load(tmp_path / f"case{ci}.npz")
+        rows = sample_rows(N, 64)
+        ref = oracle.linear_q8(data["x"], data["q"][rows], data["s"][rows], None)
+        assert rowwise_normwise_err(r[1][f"out{ci}"][:, rows], ref) <= TOL_F16, ci

@@ -667,16 +667,20 @@ int nccl_settle(b200q8_comm* c, ncclResult_t r, const char* what)
 {
     if (r == ncclSuccess) return B200Q8_OK;
     if (r != ncclInProgress) return nccl_fail(r, what);
+    // Enqueueing a collective finishes in microseconds: poll without sleeping (a sleep here
+    // would leave the GPU idle), checking the deadline now and then.
     const auto t0 = std::chrono::steady_clock::now();
-    for (;;) {
+    for (uint64_t i = 0;; i++) {
         ncclResult_t a = ncclInProgress;
         ncclResult_t q = nccl().CommGetAsyncError(c->comm, &a);
         if (q != ncclSuccess) return nccl_fail(q, "ncclCommGetAsyncError");
         if (a == ncclSuccess) return B200Q8_OK;
         if (a != ncclInProgress) return nccl_fail(a, what);
-        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-        if (el > c->timeout_s) return fail(B200Q8_ERR_TIMEOUT, "%s: still in progress after %.1f s", what, el);
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if ((i & 1023) == 1023) {
+            const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            if (el > c->timeout_s) return fail(B200Q8_ERR_TIMEOUT, "%s: still in progress after %.1f s", what, el);
+            std::this_thread::yield();
+        }
     }
 }
 
