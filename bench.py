@@ -346,26 +346,40 @@ def main():
     outs = [torch.empty((1, p * world), dtype=torch.float16, device=dev) for p in per]
 
     comm = None
+    sym = None
     if world > 1:
         uid = [v.Comm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = v.Comm(local, world, rank, uid[0], timeout_s=120.0)
+        # Outputs of the fused gather: [1, N] fp16 each, in one symmetric allocation that
+        # every peer has mapped (256-byte aligned slots).
+        offs, o = [], 0
+        for (_, N, _, _, _, _, _) in shards:
+            offs.append(o)
+            o += -(-N * 2 // 256) * 256
+        sym = comm.sym_alloc(o)
+        p2p_outs = [sym[a:a + 2 * N].view(torch.float16).view(1, N)
+                    for a, (_, N, _, _, _, _, _) in zip(offs, shards)]
 
     stream = torch.cuda.current_stream()
-    L = v.lib()
     lm_idx = [n for n, *_ in PROJ].index("lm_head")
 
-    def step(it, ev=None):
+    def step(it, ev=None, mode="p2p"):
+        """mode: "p2p" = gather fused into the GEMV (the product path for N > 1);
+        "nccl" = GEMV then NCCL all-gather; "local" = GEMV only (no gather)."""
         ws = sets[it % copies]
         for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
             q, s = ws[i]
-            slot = outs[i][:, rank * per[i]: rank * per[i] + rows]
             if ev is not None and i == lm_idx:
                 ev[0].record(stream)
-            v.linear_q8(slot, xs[i], q, s, None, stream=stream)
+            if comm is not None and mode == "p2p":
+                v.linear_q8_sharded_p2p(comm, p2p_outs[i], xs[i], q, s, None, N, stream=stream)
+            else:
+                slot = outs[i][:, rank * per[i]: rank * per[i] + rows]
+                v.linear_q8(slot, xs[i], q, s, None, stream=stream)
             if ev is not None and i == lm_idx:
                 ev[1].record(stream)
-            if comm is not None:
+            if comm is not None and mode == "nccl":
                 comm.allgather(outs[i], per[i], v.F16, stream=stream)
 
     def barrier():
@@ -403,24 +417,28 @@ def main():
     lm_bytes = algo_bytes(lm_rows, HIDDEN)
     lm_gbs = lm_bytes / (lm_ms * 1e-3) / 1e9
 
-    # ---- N > 1: the same steps without the all-gathers (compute share of the step) ---------
-    compute_only = None
+    # ---- N > 1: the same steps without any gather (compute share of the step) and with the
+    # ---- GEMV followed by a separate NCCL all-gather (the unfused alternative) ---------------
+    compute_only = nccl_leg = None
     if comm is not None:
-        saved, comm = comm, None
-        barrier()
-        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        c0.record(stream)
-        for it in range(args.steps):
-            step(it)
-        c1.record(stream)
-        barrier()
-        c_ms = c0.elapsed_time(c1)
-        t = torch.tensor([c_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        c_ms = t.item()
-        compute_only = {"value": round(total_bytes / (c_ms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
-                        "ms_per_step": round(c_ms / args.steps, 5)}
-        comm = saved
+        def leg(mode):
+            for it in range(args.warmup):
+                step(it, mode=mode)
+            barrier()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for it in range(args.steps):
+                step(it, mode=mode)
+            c1.record(stream)
+            barrier()
+            t = torch.tensor([c0.elapsed_time(c1)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            c_ms = t.item()
+            return {"value": round(total_bytes / (c_ms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(c_ms / args.steps, 5)}
+
+        compute_only = leg("local")
+        nccl_leg = leg("nccl")
 
     # ---- end to end through the C ABI with host buffers -------------------------------------
     h_in = [torch.empty((1, K), dtype=torch.float16).pin_memory() for (_, _, K, _, _, _, _) in shards]
@@ -438,10 +456,10 @@ def main():
             q, s = ws[i]
             if comm is None:
                 v.linear_q8(outs[i][:, :N], d_in[i], q, s, None, stream=stream)
+                h_out[i].copy_(outs[i][:, :N], non_blocking=True)
             else:
-                v.linear_q8_sharded(comm, outs[i][:, :N] if N % world == 0 else outs[i], d_in[i], q, s,
-                                    None, N, gather=None if N % world == 0 else outs[i], stream=stream)
-            h_out[i].copy_(outs[i][:, :N], non_blocking=True)
+                v.linear_q8_sharded_p2p(comm, p2p_outs[i], d_in[i], q, s, None, N, stream=stream)
+                h_out[i].copy_(p2p_outs[i], non_blocking=True)
 
     for it in range(args.warmup):
         e2e_step(it)
@@ -485,7 +503,8 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 weights x f16 activations, f32 accumulate", "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": 1, "activations": "fp16", "parallelism": f"column-shard x{world}",
-                       "collective": "NCCL allgather" if world > 1 else "none",
+                       "collective": "gather fused into the GEMV (peer stores over NVLink)" if world > 1
+                       else "none",
                        "l2": f"{copies} rotating weight set(s), {copies * per_rank_bytes / 1e6:.0f} MB per rank per cycle (> L2)"},
             "roofline": {"bound": "hbm", "kernel": "q8_gemv_dig_kernel (lm_head shard)", "achieved": round(lm_gbs, 2),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(lm_gbs / hbm_peak, 4),
@@ -499,6 +518,8 @@ def main():
         }
         if compute_only is not None:
             line["compute_only"] = compute_only
+        if nccl_leg is not None:
+            line["gemv_then_nccl_allgather"] = nccl_leg
         if prefill is not None:
             line["prefill"] = prefill
         if cpu_baseline is not None:
@@ -506,6 +527,8 @@ def main():
         print(json.dumps(line), flush=True)
 
     if comm is not None:
+        torch.cuda.synchronize()
+        del p2p_outs, sym
         comm.destroy()
     if world > 1:
         dist.destroy_process_group()

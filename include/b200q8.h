@@ -194,6 +194,29 @@ B200Q8_API int b200q8_linear_q8_sharded(b200q8_comm* comm, void* out, int out_dt
                              const float* bias_shard, size_t M, size_t N, size_t K, void* gather,
                              b200q8_stream_t stream);
 
+/* Symmetric device memory (collective: every rank calls it with the same
+ * `bytes`, in the same order): `bytes` of zeroed memory on this GPU, mapped
+ * into every other rank's address space (CUDA IPC over NVLink).  Freed by
+ * b200q8_comm_sym_free (collective) or with the communicator. */
+B200Q8_API int b200q8_comm_sym_alloc(b200q8_comm* comm, size_t bytes, void** local);
+B200Q8_API int b200q8_comm_sym_free(b200q8_comm* comm, void* local);
+
+/* Sharded layer with the gather fused into the GEMV: each rank's kernel stores
+ * its [M, rows] slice straight into columns [row0, row0 + rows) of `out` on
+ * EVERY rank (peer stores over NVLink), then releases a flag on each rank;
+ * a one-thread wait kernel on `stream` acquires the peers' flags (bounded:
+ * 2 s, then bit 1 of b200q8_kernel_error).  `out` [M, N] of out_dtype must
+ * lie inside one b200q8_comm_sym_alloc buffer at the same offset on every
+ * rank.  M <= 42; K % 16 == 0 and 16 <= K <= 131072; every rank must own rows.
+ * A peer may run one call ahead of this rank, so consecutive calls must use
+ * different `out` buffers (double-buffer) unless the caller has finished
+ * reading the previous result before the peers can start the next call.
+ * The first call allocates the flags (collective: all ranks make it). */
+B200Q8_API int b200q8_linear_q8_sharded_p2p(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
+                                            int in_dtype, const int8_t* w_shard, const float* scales_shard,
+                                            const float* bias_shard, size_t M, size_t N, size_t K,
+                                            b200q8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,11 +62,31 @@ def _worker(rank, world, port, path):
             v.linear_q8_sharded(comm, out, xt, qt, st, None, N, gather=gather)
         torch.cuda.synchronize()
         results[f"out{ci}"] = out.float().cpu().numpy()
+        # The gather fused into the GEMV (peer stores + flags), double-buffered in one
+        # symmetric allocation; the third call reuses buffer 0 with the same inputs.
+        for odt in (torch.float16, torch.float32):
+            eb = 2 if odt == torch.float16 else 4
+            sym = comm.sym_alloc(2 * M * N * eb)
+            bufs = [sym[i * M * N * eb:(i + 1) * M * N * eb].view(odt).view(M, N) for i in range(2)]
+            xin = xt if odt == torch.float16 else xt.float()
+            for it in range(3):
+                v.linear_q8_sharded_p2p(comm, bufs[it % 2], xin, qt, st, None, N)
+            torch.cuda.synchronize()
+            tag = "h" if odt == torch.float16 else "f"
+            results[f"p2p{tag}{ci}_0"] = bufs[0].float().cpu().numpy()
+            results[f"p2p{tag}{ci}_1"] = bufs[1].float().cpu().numpy()
+            del bufs
+            comm.sym_free(sym)
+            del sym
         if rank == 0:  # the unsharded result on one GPU
             full = torch.empty((M, N), dtype=torch.float16, device=dev)
             v.linear_q8(full, xt, torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev))
+            fullf = torch.empty((M, N), dtype=torch.float32, device=dev)
+            v.linear_q8_ex(fullf, xt.float(), torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev),
+                           algo=v.ALGO_TC_I8)
             torch.cuda.synchronize()
             results[f"full{ci}"] = full.float().cpu().numpy()
+            results[f"fullf{ci}"] = fullf.cpu().numpy()
     assert v.kernel_error() == 0
     np.savez(os.path.join(path, f"rank{rank}.npz"), **results)
     dist.barrier()
@@ -93,6 +113,11 @@ def test_sharded_two_gpus(tmp_path, oracle):
         for i in range(world):
             got = r[i][f"out{ci}"]
             assert rowwise_normwise_err(got, full) <= TOL_F16, (ci, i)
+            # The fused gather runs the same integer-exact kernel per shard: bit-identical.
+            for b in (0, 1):
+                np.testing.assert_array_equal(r[i][f"p2ph{ci}_{b}"], full, err_msg=f"case {ci} rank {i} buf {b}")
+                np.testing.assert_array_equal(r[i][f"p2pf{ci}_{b}"], r[0][f"fullf{ci}"],
+                                              err_msg=f"case {ci} rank {i} buf {b} f32")
         data = np.load(tmp_path / f"case{ci}.npz")
         rows = sample_rows(N, 64)
         ref = oracle.linear_q8(data["x"], data["q"][rows], data["s"][rows], None)

@@ -23,6 +23,7 @@ from ._lib import (  # noqa: F401
     ALGO_TC,
     ALGO_TC_I8,
     linear_q8_sharded,
+    linear_q8_sharded_p2p,
     quantize_per_channel,
     shard_range,
 )

@@ -52,6 +52,10 @@ _SIGS = {
     "b200q8_comm_allgather": ([_vp, _vp, _sz, _int, _vp], _int),
     "b200q8_linear_q8_sharded": (
         [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp], _int),
+    "b200q8_comm_sym_alloc": ([_vp, _sz, ctypes.POINTER(_vp)], _int),
+    "b200q8_comm_sym_free": ([_vp, _vp], _int),
+    "b200q8_linear_q8_sharded_p2p": (
+        [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
 }
 
 # Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
@@ -228,6 +232,7 @@ class Comm:
         self.nranks, self.rank = nranks, rank
 
     def destroy(self) -> None:
+        """Collective.  Symmetric buffers die with the communicator: drop their tensors first."""
         if self.h:
             h, self.h = self.h, None
             _check(lib().b200q8_comm_destroy(h))
@@ -235,6 +240,24 @@ class Comm:
     def allgather(self, buf, count: int, dtype: int, stream=None) -> None:
         """In place: rank r's slice is buf[r*count:(r+1)*count]."""
         _check(lib().b200q8_comm_allgather(self.h, _addr(buf), count, dtype, _stream(stream)))
+
+    def sym_alloc(self, nbytes: int):
+        """Collective: a uint8 CUDA tensor of `nbytes` zeroed bytes that every peer has mapped.
+
+        The tensor does not own the memory; it stays valid until sym_free or destroy."""
+        import torch
+
+        p = _vp()
+        _check(lib().b200q8_comm_sym_alloc(self.h, nbytes, ctypes.byref(p)))
+
+        class _Raw:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (p.value, False),
+                                        "version": 3, "strides": None}
+
+        return torch.as_tensor(_Raw(), device="cuda")
+
+    def sym_free(self, t) -> None:
+        _check(lib().b200q8_comm_sym_free(self.h, _addr(t)))
 
     def abort(self) -> None:
         if self.h:
@@ -250,3 +273,13 @@ def linear_q8_sharded(comm: Comm, out, x, w_shard, scales_shard, bias_shard, N: 
                                           _dtype_code(x), _addr(w_shard), _addr(scales_shard),
                                           _addr(bias_shard), M, N, K, _addr(gather),
                                           _stream(stream)))
+
+
+def linear_q8_sharded_p2p(comm: Comm, out, x, w_shard, scales_shard, bias_shard, N: int,
+                          stream=None) -> None:
+    """out[M,N] (all ranks) = linear_q8 over the column-sharded weight; the GEMV stores every
+    rank's slice into every rank's `out` over NVLink.  `out` lies in a Comm.sym_alloc tensor."""
+    M, K = x.shape
+    _check(lib().b200q8_linear_q8_sharded_p2p(comm.h, _addr(out), _dtype_code(out), _addr(x),
+                                              _dtype_code(x), _addr(w_shard), _addr(scales_shard),
+                                              _addr(bias_shard), M, N, K, _stream(stream)))

@@ -17,6 +17,7 @@
 #include <string>
 #include <thread>
 #include <unordered_map>
+#include <vector>
 
 #include "b200q8.h"
 #include "kernels.h"
@@ -328,11 +329,12 @@ int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, int in_dtype,
 int b200q8_kernel_error(int* code, int clear)
 {
     if (!code) return fail(B200Q8_ERR_INVALID, "kernel_error: null code");
-    int c1 = 0, c2 = 0;
+    int c1 = 0, c2 = 0, c3 = 0;
     cudaError_t e = read_kernel_error(&c1, clear != 0);
     if (e == cudaSuccess) e = read_kernel_error_i8(&c2, clear != 0);
+    if (e == cudaSuccess) e = read_kernel_error_p2p(&c3, clear != 0);
     if (e != cudaSuccess) return cuda_fail(e, "kernel_error: read device word");
-    *code = c1 | c2;
+    *code = c1 | c2 | c3;
     if (clear && *code) {
         int dev = 0;
         if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -648,10 +650,23 @@ const NcclApi& nccl()
 
 }  // namespace
 
+// Device memory allocated on every rank and mapped into every other rank's
+// address space (CUDA IPC over NVLink): peer[j] is rank j's copy.
+struct SymAlloc {
+    void* local = nullptr;
+    size_t bytes = 0;
+    void* peer[b200q8::kMaxRanks] = {};
+};
+
 struct b200q8_comm {
     ncclComm_t comm = nullptr;
     int device = 0, nranks = 1, rank = 0;
     double timeout_s = 60.0;
+    cudaStream_t xstream = nullptr;  // internal stream for handle exchanges
+    std::vector<SymAlloc> syms;
+    SymAlloc flags;                  // unsigned flags[nranks] per rank, written by the peers
+    unsigned int* done_ctr = nullptr;
+    unsigned int seq = 0;            // calls of the in-kernel gather so far (identical on all ranks)
 };
 
 namespace {
@@ -684,9 +699,115 @@ int nccl_settle(b200q8_comm* c, ncclResult_t r, const char* what)
     }
 }
 
+// All ranks' 64-byte IPC handles, gathered through the library's own NCCL communicator.
+int exchange_handles(b200q8_comm* c, const cudaIpcMemHandle_t& mine, std::vector<cudaIpcMemHandle_t>* all)
+{
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+    cudaError_t e;
+    if (!c->xstream && (e = cudaStreamCreateWithFlags(&c->xstream, cudaStreamNonBlocking)) != cudaSuccess)
+        return cuda_fail(e, "sym: stream");
+    const size_t G = (size_t)c->nranks;
+    void* d = nullptr;
+    if ((e = cudaMalloc(&d, 64 * G)) != cudaSuccess) return cuda_fail(e, "sym: exchange buffer");
+    int st = B200Q8_OK;
+    if ((e = cudaMemcpy((char*)d + 64 * c->rank, &mine, 64, cudaMemcpyHostToDevice)) != cudaSuccess)
+        st = cuda_fail(e, "sym: H2D handle");
+    if (!st) st = nccl_settle(c, nccl().AllGather((char*)d + 64 * c->rank, d, 64, ncclUint8, c->comm, c->xstream),
+                              "ncclAllGather(handles)");
+    if (!st && (e = cudaStreamSynchronize(c->xstream)) != cudaSuccess) st = cuda_fail(e, "sym: sync");
+    all->resize(G);
+    if (!st && (e = cudaMemcpy(all->data(), d, 64 * G, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        st = cuda_fail(e, "sym: D2H handles");
+    cudaFree(d);
+    return st;
+}
+
+void sym_close(b200q8_comm* c, SymAlloc* s)
+{
+    for (int j = 0; j < c->nranks; j++)
+        if (j != c->rank && s->peer[j]) cudaIpcCloseMemHandle(s->peer[j]);
+    if (s->local) cudaFree(s->local);
+    *s = SymAlloc();
+}
+
+// Collective: `bytes` of zeroed device memory on every rank, every copy mapped here.
+int sym_open(b200q8_comm* c, size_t bytes, SymAlloc* out)
+{
+    SymAlloc s;
+    s.bytes = bytes;
+    cudaError_t e;
+    if ((e = cudaMalloc(&s.local, bytes)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(B200Q8_ERR_ALLOC, "sym: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    if ((e = cudaMemset(s.local, 0, bytes)) != cudaSuccess) {
+        cudaFree(s.local);
+        return cuda_fail(e, "sym: memset");
+    }
+    cudaIpcMemHandle_t h;
+    if ((e = cudaIpcGetMemHandle(&h, s.local)) != cudaSuccess) {
+        cudaFree(s.local);
+        return cuda_fail(e, "sym: cudaIpcGetMemHandle");
+    }
+    std::vector<cudaIpcMemHandle_t> all;
+    int st = exchange_handles(c, h, &all);
+    if (st) {
+        cudaFree(s.local);
+        return st;
+    }
+    s.peer[c->rank] = s.local;
+    for (int j = 0; j < c->nranks; j++) {
+        if (j == c->rank) continue;
+        if ((e = cudaIpcOpenMemHandle(&s.peer[j], all[j], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+            s.peer[j] = nullptr;
+            sym_close(c, &s);
+            return cuda_fail(e, "sym: cudaIpcOpenMemHandle");
+        }
+    }
+    *out = s;
+    return B200Q8_OK;
+}
+
+void comm_release(b200q8_comm* c)
+{
+    for (auto& s : c->syms) sym_close(c, &s);
+    c->syms.clear();
+    if (c->flags.local) sym_close(c, &c->flags);
+    if (c->done_ctr) cudaFree(c->done_ctr);
+    c->done_ctr = nullptr;
+    if (c->xstream) cudaStreamDestroy(c->xstream);
+    c->xstream = nullptr;
+}
+
 }  // namespace
 
 extern "C" {
+
+int b200q8_comm_sym_alloc(b200q8_comm* c, size_t bytes, void** local)
+{
+    if (!c || !local || bytes == 0) return fail(B200Q8_ERR_INVALID, "comm_sym_alloc: bad arguments");
+    if (c->nranks > kMaxRanks) return fail(B200Q8_ERR_UNSUPPORTED, "comm_sym_alloc: at most %d ranks", kMaxRanks);
+    int st = set_device(c->device);
+    if (st) return st;
+    SymAlloc s;
+    if ((st = sym_open(c, bytes, &s))) return st;
+    c->syms.push_back(s);
+    *local = s.local;
+    return B200Q8_OK;
+}
+
+int b200q8_comm_sym_free(b200q8_comm* c, void* local)
+{
+    if (!c || !local) return fail(B200Q8_ERR_INVALID, "comm_sym_free: bad arguments");
+    for (size_t i = 0; i < c->syms.size(); i++) {
+        if (c->syms[i].local == local) {
+            sym_close(c, &c->syms[i]);
+            c->syms.erase(c->syms.begin() + (long)i);
+            return B200Q8_OK;
+        }
+    }
+    return fail(B200Q8_ERR_INVALID, "comm_sym_free: %p is not a symmetric allocation of this communicator", local);
+}
 
 int b200q8_shard_range(size_t N, int nranks, int rank, size_t* row0, size_t* rows)
 {
@@ -752,6 +873,7 @@ int b200q8_comm_abort(b200q8_comm* c)
 {
     if (!c) return B200Q8_OK;
     if (c->comm && nccl().loaded) nccl().CommAbort(c->comm);
+    comm_release(c);
     delete c;
     return B200Q8_OK;
 }
@@ -759,6 +881,16 @@ int b200q8_comm_abort(b200q8_comm* c)
 int b200q8_comm_destroy(b200q8_comm* c)
 {
     if (!c) return B200Q8_OK;
+    cudaDeviceSynchronize();  // this rank's stores into peers' memory are done
+    if (c->xstream) {
+        // Barrier before unmapping: a peer may still be storing into this rank's memory.
+        // Every rank has xstream iff it made the same collective symmetric allocations.
+        cudaIpcMemHandle_t none;
+        memset(&none, 0, sizeof(none));
+        std::vector<cudaIpcMemHandle_t> all;
+        exchange_handles(c, none, &all);
+    }
+    comm_release(c);
     int rc = B200Q8_OK;
     if (c->comm && nccl().loaded) {
         ncclResult_t r = nccl().CommFinalize(c->comm);
@@ -772,6 +904,83 @@ int b200q8_comm_destroy(b200q8_comm* c)
     }
     delete c;
     return rc;
+}
+
+int b200q8_linear_q8_sharded_p2p(b200q8_comm* c, void* out, int out_dtype, const void* inp, int in_dtype,
+                                 const int8_t* w_shard, const float* scales_shard, const float* bias_shard,
+                                 size_t M, size_t N, size_t K, b200q8_stream_t stream)
+{
+    if (!c) return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: null comm");
+    if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: bad dtype");
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!out || !inp || !w_shard || !scales_shard)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: null pointer");
+    const int G = c->nranks;
+    if (G > kMaxRanks) return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_sharded_p2p: at most %d ranks", kMaxRanks);
+    if (M > (size_t)gemv_i8_max_tokens())
+        return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_sharded_p2p: at most %d tokens (M=%zu)", gemv_i8_max_tokens(), M);
+    size_t row0 = 0, rows = 0, l0 = 0, lrows = 0;
+    int st = b200q8_shard_range(N, G, c->rank, &row0, &rows);
+    if (!st) st = b200q8_shard_range(N, G, G - 1, &l0, &lrows);
+    if (st) return st;
+    if (lrows == 0)  // every rank reaches the same verdict
+        return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_sharded_p2p: N=%zu leaves rank %d without rows", N, G - 1);
+    const size_t eb = out_dtype == B200Q8_F16 ? 2 : 4;
+    const SymAlloc* sym = nullptr;
+    for (const auto& s : c->syms)
+        if ((uintptr_t)out >= (uintptr_t)s.local && (uintptr_t)out + M * N * eb <= (uintptr_t)s.local + s.bytes) sym = &s;
+    if (!sym)
+        return fail(B200Q8_ERR_INVALID,
+                    "linear_q8_sharded_p2p: out must lie in a buffer from b200q8_comm_sym_alloc on this communicator");
+    if ((st = set_device(c->device))) return st;
+    cudaError_t e;
+    if (!c->flags.local) {  // first call: the flags every peer writes into (collective)
+        if ((st = sym_open(c, 256, &c->flags))) return st;
+        if ((e = cudaMalloc(&c->done_ctr, sizeof(unsigned int))) != cudaSuccess ||
+            (e = cudaMemset(c->done_ctr, 0, sizeof(unsigned int))) != cudaSuccess)
+            return cuda_fail(e, "linear_q8_sharded_p2p: counter");
+    }
+    const size_t off = (uintptr_t)out - (uintptr_t)sym->local;
+    P2POut po;
+    po.ndst = G;
+    for (int j = 0; j < G; j++) {
+        po.dst[j] = (char*)sym->peer[j] + off;
+        po.flags[j] = reinterpret_cast<unsigned int*>(c->flags.peer[j]);
+    }
+    po.ldo = (long long)N;
+    po.ocol0 = (int)row0;
+    po.done_ctr = c->done_ctr;
+    po.rank = c->rank;
+    po.seq = ++c->seq;
+    DeviceInfo d;
+    if ((st = device_info(&d))) return st;
+    LinearArgs a;
+    a.x = inp;
+    a.w = w_shard;
+    a.scales = scales_shard;
+    a.bias = bias_shard;
+    a.out = out;
+    a.M = M;
+    a.N = rows;
+    a.K = K;
+    a.in_dtype = in_dtype;
+    a.out_dtype = out_dtype;
+    a.pdl = true;
+    a.p2p = &po;
+    if (!gemv_i8_supports(a))
+        return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_sharded_p2p: needs K %% 16 == 0, 16 <= K <= 131072 and "
+                                            "aligned pointers (K=%zu)", K);
+    ScratchNeed need;
+    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+    TcScratch scratch;
+    if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
+    if ((e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream)) != cudaSuccess)
+        return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");
+    if ((e = launch_p2p_wait(reinterpret_cast<unsigned int*>(c->flags.local), G, c->rank, po.seq,
+                             2000000000ull, (cudaStream_t)stream)) != cudaSuccess)
+        return cuda_fail(e, "linear_q8_sharded_p2p: wait launch");
+    return B200Q8_OK;
 }
 
 int b200q8_comm_allgather(b200q8_comm* c, void* buf, size_t count, int dtype, b200q8_stream_t stream)

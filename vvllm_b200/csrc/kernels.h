@@ -9,6 +9,23 @@ namespace b200q8 {
 
 enum DType : int { kF32 = 0, kF16 = 1 };
 
+// Output placement for the column-sharded path with an in-kernel gather: every
+// output element is stored into `ndst` copies of the full [M, ldo] output
+// (the local one and each peer's, mapped over NVLink), at column ocol0 + row.
+// When the last CTA of the launch is done it writes `seq` into flags[rank] of
+// every rank (system-scope release); peers wait for it before reading.
+constexpr int kMaxRanks = 8;
+struct P2POut {
+    int ndst = 1;
+    void* dst[kMaxRanks] = {};
+    long long ldo = 0;
+    int ocol0 = 0;
+    unsigned int* done_ctr = nullptr;          // local, zero between launches
+    unsigned int* flags[kMaxRanks] = {};        // flags array base on every rank
+    int rank = 0;
+    unsigned int seq = 0;
+};
+
 struct LinearArgs {
     const void* x = nullptr;        // [M, K] activations (in_dtype)
     const int8_t* w = nullptr;      // [N, K] int8, row-major
@@ -19,7 +36,14 @@ struct LinearArgs {
     size_t M = 0, N = 0, K = 0;
     int in_dtype = kF32, out_dtype = kF32;
     bool pdl = false;               // launch with programmatic stream serialization
+    const P2POut* p2p = nullptr;    // int8 digit GEMV only: gather into peers' outputs
 };
+
+// One thread waits (bounded, `timeout_ns`) until flags[j] == seq for every rank j != rank;
+// on expiry it sets bit 1 of the device error word and returns.
+cudaError_t launch_p2p_wait(const unsigned int* flags, int nranks, int rank, unsigned int seq,
+                            unsigned long long timeout_ns, cudaStream_t stream);
+cudaError_t read_kernel_error_p2p(int* code, bool clear);
 
 // Streaming SIMT GEMV, M <= gemv_max_tokens().  Also takes any M/K through a
 // generic (slow, correct) kernel when the fast one cannot (alignment, K % 16).

@@ -77,6 +77,7 @@ struct DigParams {
     int M, N, K;
     int kbpt;
     long long units;
+    P2POut po;        // output placement: local only (ndst = 1) or every rank's copy
 };
 
 template <int NC, int BK, int S>
@@ -171,13 +172,17 @@ __device__ __forceinline__ float recombine(const long long (&dsum)[kDigits], int
     return __double2float_rn(ldexp(acc, -e));
 }
 
+// v = acc * scale (+ bias) (+ res[m, n]) stored at column ocol0 + n of row m in every
+// output copy (one local copy, or each rank's copy over NVLink for the sharded gather).
 template <typename OT>
-__device__ __forceinline__ void epi_one(OT* o, const OT* res, float acc, float scale, float bias, bool has_bias)
+__device__ __forceinline__ void epi_out(const DigParams& p, int m, int n, float acc, float scale, float bias,
+                                        bool has_bias)
 {
     float v = __fmul_rn(acc, scale);
     if (has_bias) v = __fadd_rn(v, bias);
-    if (res) v = __fadd_rn(v, load_as_f32<OT>(res));
-    sk::store_out<OT>(o, v);
+    if (p.res) v = __fadd_rn(v, load_as_f32<OT>(reinterpret_cast<const OT*>(p.res) + (size_t)m * p.N + n));
+    const size_t o = (size_t)m * p.po.ldo + p.po.ocol0 + n;
+    for (int d = 0; d < p.po.ndst; d++) sk::store_out<OT>(reinterpret_cast<OT*>(p.po.dst[d]) + o, v);
 }
 
 // ----------------------------------------------------------------------------- GEMV
@@ -427,9 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 long long ds[kDigits];
 #pragma unroll
                                 for (int i = 0; i < kDigits; i++) ds[i] = dreg[tt * kDigits + i];
-                                const size_t o = (size_t)m * p.N + n;
-                                epi_one<OT>(out + o, res ? res + o : nullptr, recombine(ds, p.exps[m]), scale, bias,
-                                            has_bias);
+                                epi_out<OT>(p, m, n, recombine(ds, p.exps[m]), scale, bias, has_bias);
                             }
                         }
                     }
@@ -467,11 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int i = 0; i < kDigits; i++) ds[i] += __ldcg(pj + i);
                         }
-                        if (nv) {
-                            const size_t o = (size_t)m * p.N + n;
-                            epi_one<OT>(out + o, res ? res + o : nullptr, recombine(ds, p.exps[m]), scale, bias,
-                                        has_bias);
-                        }
+                        if (nv) epi_out<OT>(p, m, n, recombine(ds, p.exps[m]), scale, bias, has_bias);
                     }
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                     if (etid == 0) p.counters[t] = 0;
@@ -490,6 +489,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, C::kTmemCols);
+    }
+    if (p.po.done_ctr && threadIdx.x == 0) {
+        // The last CTA to finish publishes this rank's slice to every rank: flags[r][rank] = seq.
+        // The barrier above orders every thread's output stores (local and peer) before this
+        // thread's system-scope fence, which makes them visible before the counter moves.
+        __threadfence_system();
+        const unsigned int prev = atomicAdd(p.po.done_ctr, 1u);
+        if (prev == gridDim.x - 1) {
+            *p.po.done_ctr = 0;  // ready for the next launch
+            __threadfence_system();
+            if (atomicAdd(&g_kernel_error_i8, 0) == 0) {  // a timed-out launch publishes nothing
+                // this rank's own flag last: once it is seen, the launch has no stores left
+                for (int i = 1; i <= p.po.ndst; i++) {
+                    const int d = (p.po.rank + i) % p.po.ndst;
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.po.flags[d] + p.po.rank),
+                                 "r"(p.po.seq)
+                                 : "memory");
+                }
+            }
+        }
     }
 }
 
@@ -584,6 +603,15 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.kbpt = (int)((a.K + BK - 1) / BK);
     const long long tiles = (long long)((a.N + kTileRows - 1) / kTileRows);
     p.units = tiles * p.kbpt;
+    if (a.p2p) {
+        p.po = *a.p2p;
+    } else {  // one local [M, N] output
+        p.po = P2POut();
+        p.po.ndst = 1;
+        p.po.dst[0] = a.out;
+        p.po.ldo = (long long)a.N;
+        p.po.ocol0 = 0;
+    }
     const int G = (int)((p.units < num_sms) ? p.units : num_sms);
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
         sc.exps_count < a.M)
