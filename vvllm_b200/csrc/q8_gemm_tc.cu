@@ -5,28 +5,34 @@
 //  src/backend/backend_naive.cc:155-291 and :322-335, with fp16 activations.)
 //
 // Tiling ("swap-AB"): a tile is 128 weight rows (UMMA M) x BN tokens (UMMA N,
-// 16..128), so one kernel serves M = 1 decode through M = 512 prefill.  K
-// runs in BK-wide pipeline stages (256 for decode tiles, 128 for wide token
-// tiles); each stage carries BK/16 tcgen05.mma instructions, enough work to
-// hide the per-stage control cost of the single issuing thread.
+// 16..256), so one kernel serves M = 1 decode through M >= 512 prefill.  K
+// runs in BK-wide pipeline stages.  One tcgen05.mma takes a fixed ~45-70
+// cycles to issue from the single issuing thread, so wide prefill tiles use
+// UMMA N = 256 (128 cycles of tensor work per instruction) to keep the tensor
+// pipe, not the issuing thread, the limit.
 //
 // Persistent stream-K schedule: the (tile, K-stage) units of the whole problem
 // are laid out tile-major and cut into gridDim.x equal contiguous ranges, one
 // per CTA (one CTA per SM).  A CTA works on a few whole tiles plus at most two
 // partial tiles at the ends of its range; skinny shapes (few tiles, long K)
 // still keep every SM busy, and no wave is left half-empty.  A tile split over
-// several CTAs is finished deterministically: each piece stores its fp32
-// partial accumulator to a workspace slot, bumps the tile's counter, and the
-// piece that arrives last sums all pieces in K order, applies the epilogue and
-// resets the counter.  No CTA ever waits on another.
+// several CTAs is finished deterministically by the piece that arrives last:
+// a piece that finds every other piece already arrived keeps its accumulator in
+// tensor memory and skips its workspace round trip; otherwise it stores its
+// fp32 partial to a workspace slot (float4-interleaved by row, so a warp's
+// stores and loads are contiguous) and bumps the tile's counter.  The last
+// piece sums all pieces in K order (its own straight from TMEM), applies the
+// epilogue and resets the counter.  No CTA ever waits on another.
 //
 // Warp roles (14 warps):
-//   0      TMA producer: int8 weight tile [128 x BK] as 128-byte-swizzled
-//          [128 x 128 B] boxes and fp16 activation tile [BN x BK] as
-//          128-byte-swizzled [BN x 64] boxes into an S-stage shared-memory
-//          ring, completing on mbarriers;
+//   0      TMA producer: int8 weight tile [128 x BK] as swizzled boxes of
+//          [128 rows x min(BK,128) B] (64- or 128-byte swizzle) and fp16
+//          activation tile [BN x BK] as 128-byte-swizzled [BN x 64] boxes into
+//          an S-stage shared-memory ring, completing on mbarriers.  The weight
+//          boxes of the first stages are requested before the programmatic
+//          dependency wait (weights do not depend on the previous kernel);
 //   1      TMEM allocator; one thread issues tcgen05.mma.kind::f16
-//          [D_tmem], [A_tmem], B_desc into one of two TMEM accumulators, and
+//          [D_tmem], [A_tmem], B_desc into one of kAcc TMEM accumulators, and
 //          tcgen05.commit frees the stages;
 //   2..9   dequantizers in two groups taking alternate stages: a thread owns
 //          one weight row (= TMEM lane), reads its BK int8 from shared memory
@@ -50,6 +56,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_utils.cuh"
+#include "tmap.cuh"
 
 namespace b200q8 {
 
@@ -68,47 +75,52 @@ struct SkParams {
     const float* bias;
     const void* res;
     void* out;
-    float* ws;          // [2 * gridDim.x][BN][128] fp32 partial accumulators
+    float* ws;          // [2 * gridDim.x] slots of [BN / 4][128][4] fp32 partial accumulators
     int* counters;      // [tiles] arrival counters, zero between launches
     int M, N, K;
     int kbpt;           // K stages per tile
     int tiles_n;        // weight-row tiles
     long long units;    // tiles * kbpt
+    int tma_out;        // outputs leave by TMA store (16-byte aligned rows), else direct stores
 };
 
 template <int BN, int BK, int S, int SA>
 struct SkCfg {
-    static constexpr int kWBoxes = BK / 128;            // [128 rows x 128 B] int8 boxes per stage
-    static constexpr int kXBoxes = BK / 64;             // [BN rows x 64 fp16] boxes per stage
+    static constexpr int kWBoxW = BK < 128 ? BK : 128;  // bytes per weight-box row
+    static constexpr int kWBoxes = BK / kWBoxW;
+    static constexpr int kWBoxBytes = kTileRows * kWBoxW;
     static constexpr int kW8Bytes = kTileRows * BK;
+    static constexpr int kXBoxes = BK / 64;             // [BN rows x 64 fp16] boxes per stage
     static constexpr int kXBoxBytes = BN * 128;
     static constexpr int kXBytes = kXBoxes * kXBoxBytes;
     static constexpr int kACols = BK / 2;               // TMEM columns of one A stage
     static constexpr int kDCols = (BN + 31) / 32 * 32;  // one accumulator, 32-column aligned
-    static constexpr int kACol = 2 * kDCols;
+    static constexpr int kAcc = (2 * kDCols + SA * kACols <= 512) ? 2 : 1;
+    static constexpr int kACol = kAcc * kDCols;
     static constexpr int kColsNeeded = kACol + SA * kACols;
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                      : kColsNeeded <= 256 ? 256 : 512;
-    static constexpr int kNumBars = 2 * S + 2 * SA + 4 + 1;  // + accfull[2], accempty[2], drain
-    static constexpr int kSmemBytes = 1024 + S * (kW8Bytes + kXBytes) + kNumBars * 8 + 16;
+    static constexpr int kChunk = BN < 32 ? BN : 32;    // accumulator columns per tcgen05.ld in the epilogue
+    static constexpr int kNumBars = 2 * S + 2 * SA + 2 * kAcc + 2;  // + accfull/accempty[kAcc], drain, fixup
+    static constexpr int kOutBufBytes = kChunk * kTileRows * 4;  // one staged chunk (fp32 or fp16 outputs, fp32 partials)
+    static constexpr int kSmemBytes = 1024 + S * (kW8Bytes + kXBytes) + 2 * kOutBufBytes + kNumBars * 8 + 16;
     static_assert(kColsNeeded <= 512, "TMEM overflow");
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "UMMA N for M=128, two accumulators");
-    static_assert(BK % 128 == 0, "stage K is whole 128-byte weight boxes");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M = 128");
+    static_assert(BK == 64 || BK % 128 == 0, "stage K is one 64-byte box or whole 128-byte boxes");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
-    static_assert(kXBoxBytes % 1024 == 0, "activation boxes stay 1024-byte aligned");
+    static_assert(kXBoxBytes % 1024 == 0 && kW8Bytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(BN % kChunk == 0, "epilogue chunks tile the accumulator");
 };
 
-template <typename OT>
-__device__ __forceinline__ void store_out(OT* p, float v);
-template <>
-__device__ __forceinline__ void store_out<float>(float* p, float v)
+// Byte offset of 16-byte chunk c of row r inside a weight box, under the box's
+// TMA swizzle (128-byte rows: chunk ^= r & 7; 64-byte rows: chunk ^= (r >> 1) & 3).
+template <int kBoxW>
+__device__ __forceinline__ int wchunk(int r, int c)
 {
-    *p = v;
-}
-template <>
-__device__ __forceinline__ void store_out<__half>(__half* p, float v)
-{
-    *p = __float2half_rn(v);
+    if constexpr (kBoxW == 128)
+        return r * 128 + ((c ^ (r & 7)) << 4);
+    else
+        return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
 }
 
 __device__ __forceinline__ void raise_error(volatile int* abort)
@@ -158,60 +170,60 @@ struct Ring {
     }
 };
 
-// Epilogue of up to 16 consecutive tokens of one output channel: element i goes to
-// o[i * ld]; v = acc * scale (+ bias) (+ res), in the reference's order.
-template <typename OT>
-__device__ __forceinline__ void epi_chunk(OT* o, const OT* res, int ld, int cnt, const uint32_t (&d)[16], float scale,
-                                          float bias, bool has_bias)
+// CH accumulator columns of this thread's TMEM lane, starting at column `col`.
+template <int CH>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t col, float (&v)[CH])
 {
-    if (cnt == 16) {
+    if constexpr (CH == 32) {
+        uint32_t d[32];
+        tc::tmem_ld_32x32b_x32(col, d);
+        tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            float v = __fmul_rn(__uint_as_float(d[i]), scale);
-            if (has_bias) v = __fadd_rn(v, bias);
-            if (res) v = __fadd_rn(v, load_as_f32<OT>(res + (size_t)i * ld));
-            store_out<OT>(o + (size_t)i * ld, v);
-        }
+        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(d[i]);
     } else {
+        static_assert(CH == 16, "chunk of 16 or 32 columns");
+        uint32_t d[16];
+        tc::tmem_ld_32x32b_x16(col, d);
+        tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            if (i < cnt) {
-                float v = __fmul_rn(__uint_as_float(d[i]), scale);
-                if (has_bias) v = __fadd_rn(v, bias);
-                if (res) v = __fadd_rn(v, load_as_f32<OT>(res + (size_t)i * ld));
-                store_out<OT>(o + (size_t)i * ld, v);
-            }
-        }
+        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(d[i]);
     }
 }
 
 template <int BN, int BK, int S, int SA, typename OT>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_gemm_sk_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                      const SkParams p)
+                      const __grid_constant__ CUtensorMap tmO, const SkParams p)
 {
     using C = SkCfg<BN, BK, S, SA>;
+    constexpr int CH = C::kChunk;
+    constexpr int kRedSlotBytes = kTileRows * CH * 4;  // one piece's CH-column chunk
+    constexpr int kRedSlots = S * (C::kW8Bytes + C::kXBytes) / kRedSlotBytes;
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~static_cast<uintptr_t>(1023));
     unsigned char* sW8 = smem;
     unsigned char* sX = smem + S * C::kW8Bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + S * C::kXBytes);
+    unsigned char* sOut = sX + S * C::kXBytes;  // two output staging buffers
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 2 * C::kOutBufBytes);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]: first / last segment
 
     const uint32_t bar0 = tc::smem_u32(bars);
     const uint32_t full0 = bar0, empty0 = bar0 + 8u * S, afull0 = bar0 + 16u * S,
                    aempty0 = bar0 + 16u * S + 8u * SA, accfull0 = bar0 + 16u * S + 16u * SA,
-                   accempty0 = accfull0 + 16u, drainbar = accfull0 + 32u;
+                   accempty0 = accfull0 + 8u * C::kAcc, drainbar = accempty0 + 8u * C::kAcc,
+                   redbar = drainbar + 8u;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int G = gridDim.x;
     const int cta = blockIdx.x;
     const long long u_begin = unit_begin(cta, p.units, G), u_end = unit_begin(cta + 1, p.units, G);
+    const uint32_t sw_base = tc::smem_u32(sW8), sx_base = tc::smem_u32(sX), sout_base = tc::smem_u32(sOut);
 
+    int pre = 0;  // stages whose weight boxes were requested before the dependency wait
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             tc::mbar_init(full0 + 8u * s, 1);
@@ -221,17 +233,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mbar_init(afull0 + 8u * s, 4);
             tc::mbar_init(aempty0 + 8u * s, 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < C::kAcc; b++) {
             tc::mbar_init(accfull0 + 8u * b, 1);
             tc::mbar_init(accempty0 + 8u * b, 4);
         }
         tc::mbar_init(drainbar, 1);
+        tc::mbar_init(redbar, 1);
         *abort = 0;
         tc::fence_mbar_init();
-    }
-    if (threadIdx.x == 32) {
+        // Weights do not depend on the previous kernel: start streaming them now.
         tc::prefetch_tensormap(&tmW);
         tc::prefetch_tensormap(&tmX);
+        tc::prefetch_tensormap(&tmO);
+        int t, k0, k1;
+        SegIter it(u_begin, u_end, p.kbpt);
+        while (pre < S && it.next(t, k0, k1)) {
+            const int row0 = (t % p.tiles_n) * kTileRows;
+            for (int kb = k0; kb < k1 && pre < S; kb++, pre++) {
+                const uint32_t fb = full0 + 8u * pre;
+                tc::mbar_arrive_expect_tx(fb, C::kW8Bytes + C::kXBytes);
+#pragma unroll
+                for (int h = 0; h < C::kWBoxes; h++)
+                    tc::tma_load_2d(sw_base + pre * C::kW8Bytes + h * C::kWBoxBytes, &tmW, kb * BK + h * C::kWBoxW,
+                                    row0, fb);
+            }
+        }
     }
     // Activations come from the previous kernel; hold no TMEM while waiting for it.
     pdl_wait();
@@ -253,24 +279,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             int t, k0, k1;
             SegIter it(u_begin, u_end, p.kbpt);
             bool ok = true;
-            const uint32_t sw_base = tc::smem_u32(sW8), sx_base = tc::smem_u32(sX);
             while (ok && it.next(t, k0, k1)) {
                 const int row0 = (t % p.tiles_n) * kTileRows;
                 const int m0 = (t / p.tiles_n) * BN;
                 for (int kb = k0; kb < k1; kb++) {
-                    if (issued >= S &&
-                        !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
-                        raise_error(abort);
-                        ok = false;
-                        break;
-                    }
                     const uint32_t fb = full0 + 8u * st.idx;
-                    tc::mbar_arrive_expect_tx(fb, C::kW8Bytes + C::kXBytes);
-                    const uint32_t wdst = sw_base + st.idx * C::kW8Bytes;
-                    const uint32_t xdst = sx_base + st.idx * C::kXBytes;
+                    if (issued >= pre) {
+                        if (issued >= S &&
+                            !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
+                            raise_error(abort);
+                            ok = false;
+                            break;
+                        }
+                        tc::mbar_arrive_expect_tx(fb, C::kW8Bytes + C::kXBytes);
 #pragma unroll
-                    for (int h = 0; h < C::kWBoxes; h++)
-                        tc::tma_load_2d(wdst + h * (kTileRows * 128), &tmW, kb * BK + h * 128, row0, fb);
+                        for (int h = 0; h < C::kWBoxes; h++)
+                            tc::tma_load_2d(sw_base + st.idx * C::kW8Bytes + h * C::kWBoxBytes, &tmW,
+                                            kb * BK + h * C::kWBoxW, row0, fb);
+                    }
+                    const uint32_t xdst = sx_base + st.idx * C::kXBytes;
 #pragma unroll
                     for (int h = 0; h < C::kXBoxes; h++)
                         tc::tma_load_2d(xdst + h * C::kXBoxBytes, &tmX, kb * BK + h * 64, m0, fb);
@@ -282,8 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // drain: every copy this CTA issued lands before the CTA exits
                 const int zero = 0;
                 Ring d;
-                for (int q = 0; q < issued; q++, d.next(S))
-                    if (q + S >= issued) tc::mbar_wait(full0 + 8u * d.idx, d.phase, &zero, kWaitTimeoutNs);
+                const int requested = issued > pre ? issued : pre;
+                for (int q = 0; q < requested; q++, d.next(S))
+                    if (q + S >= requested) tc::mbar_wait(full0 + 8u * d.idx, d.phase, &zero, kWaitTimeoutNs);
             }
         }
     } else if (warp == 1) {
@@ -296,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             const uint64_t bdesc0 = tc::make_sw128_kmajor_desc(tc::smem_u32(sX));
             while (ok && it.next(t, k0, k1)) {
-                const int ab = seg & 1, use = seg >> 1;
+                const int ab = seg % C::kAcc, use = seg / C::kAcc;
                 if (use > 0 &&
                     !tc::mbar_wait(accempty0 + 8u * ab, (uint32_t)((use - 1) & 1), abort, kWaitTimeoutNs)) {
                     raise_error(abort);
@@ -341,7 +369,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;                       // TMEM lane quadrant this warp may access
         const int r = q * 32 + lane;
         const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-        const int sw = r & 7;  // 128-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ (r & 7)
         Ring st, sa;
         int g = 0;
         int t, k0, k1;
@@ -358,18 +385,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                 }
                 tc::tc_fence_after();
-                const unsigned char* rowp = sW8 + st.idx * C::kW8Bytes + r * 128;
+                const unsigned char* wst = sW8 + st.idx * C::kW8Bytes;
                 const uint32_t a_col = tmem + t_lane + C::kACol + sa.idx * C::kACols;
 #pragma unroll
                 for (int h = 0; h < C::kWBoxes; h++) {
-                    // 128 int8 of this row -> 64 packed half2 -> TMEM columns [64h, 64h + 64)
+                    // 64 int8 of this row -> 32 packed half2 -> 32 TMEM columns
 #pragma unroll
-                    for (int half = 0; half < 2; half++) {
+                    for (int half = 0; half < C::kWBoxW / 64; half++) {
                         uint4 v[4];
 #pragma unroll
                         for (int j = 0; j < 4; j++)
-                            v[j] = *reinterpret_cast<const uint4*>(rowp + h * (kTileRows * 128) +
-                                                                   (((half * 4 + j) ^ sw) << 4));
+                            v[j] = *reinterpret_cast<const uint4*>(wst + h * C::kWBoxBytes +
+                                                                   wchunk<C::kWBoxW>(r, half * 4 + j));
                         uint32_t hh[32];
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
@@ -378,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tc::i8x4_to_h2x2(v[j].z, hh[8 * j + 4], hh[8 * j + 5]);
                             tc::i8x4_to_h2x2(v[j].w, hh[8 * j + 6], hh[8 * j + 7]);
                         }
-                        tc::tmem_st_32x32b_x32(a_col + h * 64 + half * 32, hh);
+                        tc::tmem_st_32x32b_x32(a_col + h * (C::kWBoxW / 2) + half * 32, hh);
                     }
                 }
                 tc::tmem_st_wait();
@@ -394,116 +421,223 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = q * 32 + lane;
         const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
         const int etid = threadIdx.x - kFirstEpi * 32;  // 0..127
+        const bool has_bias = p.bias != nullptr;
+        uint32_t redphase = 0;
+        int nstore = 0;  // chunks staged so far (selects the staging buffer)
         int seg = 0, t, k0, k1;
         SegIter it(u_begin, u_end, p.kbpt);
         bool ok = true;
-        while (it.next(t, k0, k1)) {
-            const int ab = seg & 1, use = seg >> 1;
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
-            if (!ok) break;
-            tc::tc_fence_after();
+        // One chunk of outputs (tokens m .. m + CH - 1 of this thread's channel) goes
+        // through a staging buffer in shared memory and leaves with one TMA store;
+        // rows and columns beyond the output's extent are clipped by the store.
+        // One chunk of outputs (tokens m .. m + cnt - 1 of this thread's channel): the epilogue
+        // math runs branch-free over the whole chunk (warp-uniform choices are made once per
+        // chunk; per-element conditions in an unrolled loop cost a reconvergence point each),
+        // then the chunk goes through a staging buffer in shared memory and leaves with one
+        // TMA store, which clips rows and columns beyond the output's extent.
+        auto out_chunk = [&](const float (&v)[CH], int n0, int m, int cnt, float scale, float bias, const OT* rres) {
+            float y[CH];
+            if (has_bias) {
+#pragma unroll
+                for (int i = 0; i < CH; i++) y[i] = __fadd_rn(__fmul_rn(v[i], scale), bias);
+            } else {
+#pragma unroll
+                for (int i = 0; i < CH; i++) y[i] = __fmul_rn(v[i], scale);
+            }
+            if (rres) {
+                // rows past the output's end re-read its last row (in range) and are not stored
+#pragma unroll
+                for (int i = 0; i < CH; i++) {
+                    const float rv = load_as_f32<OT>(rres + (size_t)min(i, cnt - 1) * p.N);
+                    y[i] = i < cnt ? __fadd_rn(y[i], rv) : y[i];
+                }
+            }
+            if (!p.tma_out) {  // output rows not 16-byte aligned: direct stores
+                if (n0 + r < p.N) {
+                    OT* o = reinterpret_cast<OT*>(p.out) + (size_t)m * p.N + n0 + r;
+#pragma unroll
+                    for (int i = 0; i < CH; i++)
+                        if (i < cnt) store_from_f32<OT>(o + (size_t)i * p.N, y[i]);
+                }
+                return;
+            }
+            const int b = nstore & 1;
+            if (etid == 0) tc::bulk_wait_read<1>();  // the store that used buffer b is done reading it
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            OT* buf = reinterpret_cast<OT*>(sOut + b * C::kOutBufBytes);
+#pragma unroll
+            for (int i = 0; i < CH; i++) store_from_f32<OT>(buf + i * kTileRows + r, y[i]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (etid == 0) {
+                tc::tma_store_2d(&tmO, sout_base + b * C::kOutBufBytes, n0, m);
+                tc::bulk_commit();
+            }
+            nstore++;
+        };
+        const float4* stage = reinterpret_cast<const float4*>(smem);  // staged pieces (mode 2)
+        // Fixup piece j's slot: CTA j's first-segment slot (2j) if its range starts inside this
+        // tile, else its last-segment slot (2j + 1).
+        auto piece_slot = [&](int j, long long tb) -> const float* {
+            const int sj = (unit_begin(j, p.units, G) >= tb) ? 2 * j : 2 * j + 1;
+            return p.ws + (size_t)sj * kTileRows * BN;
+        };
+        while (ok && it.next(t, k0, k1)) {
+            const int ab = seg % C::kAcc, use = seg / C::kAcc;
             const int row0 = (t % p.tiles_n) * kTileRows;
             const int m0 = (t / p.tiles_n) * BN;
             const int mvalid = min(BN, p.M - m0);
+            const int nchunks = (mvalid + CH - 1) / CH;
             const int n = row0 + r;
             const bool nv = n < p.N;
             const float scale = nv ? p.scales[n] : 0.0f;
-            const float bias = (nv && p.bias) ? p.bias[n] : 0.0f;
+            const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
+            const OT* rrow = (p.res && nv) ? reinterpret_cast<const OT*>(p.res) + (size_t)m0 * p.N + n : nullptr;
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            if (!ok) break;
+            tc::tc_fence_after();
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
+            const long long tb = (long long)t * p.kbpt;
             const bool whole = (k0 == 0 && k1 == p.kbpt);
-            const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
-            // workspace slot layout: [128 rows][BN tokens] fp32, so a row's partials are contiguous
-            float* wrow = p.ws + ((size_t)slot * kTileRows + r) * BN;
-            OT* orow = reinterpret_cast<OT*>(p.out) + (size_t)m0 * p.N + n;
-            const OT* rrow = p.res ? reinterpret_cast<const OT*>(p.res) + (size_t)m0 * p.N + n : nullptr;
+            const int j0 = whole ? cta : cta_of_unit(tb, p.units, G);
+            const int j1 = whole ? cta : cta_of_unit(tb + p.kbpt - 1, p.units, G);
+            const int others = j1 - j0;  // pieces of other CTAs
+            const int before = cta - j0;  // of them, those that precede this CTA's piece in K
+            volatile int* lf = last_flag + (seg == 0 ? 0 : 1);
+            // mode: 0 = write the output, 1 = store this piece's partial, 2 = reduce staged
+            // pieces (bulk copies into the idle pipeline smem), 3 = reduce pieces read from
+            // the workspace (pipeline still busy).  One loop serves all four, so the store
+            // and reduction code is shared and stays warm in the instruction cache.
+            int mode = 0;
+            if (!whole) {
+                if (etid == 0) {
+                    int seen;
+                    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(p.counters + t) : "memory");
+                    *lf = (seen == others) ? 1 : 0;  // every other piece is in already
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                mode = *lf ? 2 : 1;
+            }
+            for (int pass = 0; pass < 2 && ok; pass++) {
+                if (mode == 2) {
+                    __threadfence();  // acquire: the other pieces' partials
+                    if (!(it.u >= it.end && others <= kRedSlots)) mode = 3;
+                }
+                const int per_batch = mode == 2 ? kRedSlots / others : nchunks;
+                float* my_slot = p.ws + (size_t)(seg == 0 ? 2 * cta : 2 * cta + 1) * kTileRows * BN;
 #pragma unroll 1
-            for (int c0 = 0; c0 < mvalid; c0 += 16) {
-                uint32_t d[16];
-                __syncwarp();
-                tc::tmem_ld_32x32b_x16(d_tmem + c0, d);
-                tc::tmem_ld_wait();
-                if (whole) {
-                    if (nv) epi_chunk<OT>(orow + (size_t)c0 * p.N, rrow ? rrow + (size_t)c0 * p.N : nullptr, p.N,
-                                          min(16, mvalid - c0), d, scale, bias, p.bias != nullptr);
-                } else {
-                    float4* w4 = reinterpret_cast<float4*>(wrow + c0);
+                for (int cb = 0; cb < nchunks; cb += per_batch) {
+                    const int ce = min(nchunks, cb + per_batch);
+                    if (mode == 2) {
+                        if (etid == 0) {
+                            // the batch before was read by every thread (barrier below); order
+                            // those reads and the partials' acquire before the copies
+                            asm volatile("fence.proxy.async;" ::: "memory");
+                            tc::mbar_arrive_expect_tx(redbar, (uint32_t)((ce - cb) * others * kRedSlotBytes));
+                            int slot = 0;
+                            for (int c = cb; c < ce; c++)
+                                for (int j = j0; j <= j1; j++) {
+                                    if (j == cta) continue;
+                                    tc::bulk_load(sw_base + slot * kRedSlotBytes, piece_slot(j, tb) + (size_t)c * kTileRows * CH,
+                                                  kRedSlotBytes, redbar);
+                                    slot++;
+                                }
+                        }
+                        ok = __all_sync(0xffffffffu, tc::mbar_wait(redbar, redphase, abort, kWaitTimeoutNs));
+                        redphase ^= 1u;
+                        if (!ok) {  // let the copies in flight land before the CTA can exit
+                            const int zero = 0;
+                            tc::mbar_wait(redbar, redphase ^ 1u, &zero, kWaitTimeoutNs);
+                            break;
+                        }
+                    }
+#pragma unroll 1
+                    for (int c = cb; c < ce; c++) {
+                        const int c0 = c * CH;
+                        float acc[CH];
+                        if (mode < 2) {
+                            __syncwarp();
+                            tmem_ld_chunk<CH>(d_tmem + c0, acc);
+                        } else {
+                            // pieces in K order: those before this CTA's, its own (from TMEM), the rest
+                            const float4* sp = mode == 2 ? stage + (size_t)((c - cb) * others) * (kRedSlotBytes / 16) + r
+                                                         : nullptr;
 #pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        __stcg(w4 + i, make_float4(__uint_as_float(d[4 * i]), __uint_as_float(d[4 * i + 1]),
-                                                   __uint_as_float(d[4 * i + 2]), __uint_as_float(d[4 * i + 3])));
+                            for (int i = 0; i < CH; i++) acc[i] = 0.0f;
+#pragma unroll 1
+                            for (int k = 0; k <= others; k++) {
+                                if (k == before) {
+                                    float own[CH];
+                                    __syncwarp();
+                                    tmem_ld_chunk<CH>(d_tmem + c0, own);
+#pragma unroll
+                                    for (int i = 0; i < CH; i++) acc[i] = before > 0 ? acc[i] + own[i] : own[i];
+                                }
+                                if (k == others) break;
+                                const float4* src = mode == 2 ? sp + (size_t)k * (kRedSlotBytes / 16)
+                                                              : reinterpret_cast<const float4*>(piece_slot(j0 + k + (k >= before ? 1 : 0), tb)) +
+                                                                    (size_t)(c0 >> 2) * kTileRows + r;
+#pragma unroll
+                                for (int i = 0; i < CH / 4; i++) {
+                                    const float4 q4 = mode == 2 ? src[i * kTileRows] : __ldcg(src + i * kTileRows);
+                                    acc[4 * i] += q4.x;
+                                    acc[4 * i + 1] += q4.y;
+                                    acc[4 * i + 2] += q4.z;
+                                    acc[4 * i + 3] += q4.w;
+                                }
+                            }
+                        }
+                        if (mode == 1) {
+                            // partial -> this CTA's workspace slot through a staging buffer
+                            const int b = nstore & 1;
+                            if (etid == 0) tc::bulk_wait_read<1>();
+                            asm volatile("bar.sync 1, 128;" ::: "memory");
+                            float4* buf = reinterpret_cast<float4*>(sOut + b * C::kOutBufBytes);
+#pragma unroll
+                            for (int i = 0; i < CH / 4; i++)
+                                buf[i * kTileRows + r] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            asm volatile("bar.sync 1, 128;" ::: "memory");
+                            if (etid == 0) {
+                                tc::bulk_store(my_slot + (size_t)c0 * kTileRows, sout_base + b * C::kOutBufBytes,
+                                               (uint32_t)(CH * kTileRows * 4));
+                                tc::bulk_commit();
+                            }
+                            nstore++;
+                        } else {
+                            out_chunk(acc, row0, m0 + c0, min(CH, mvalid - c0), scale, bias,
+                                      rrow ? rrow + (size_t)c0 * p.N : nullptr);
+                        }
+                    }
+                    if (mode == 2) asm volatile("bar.sync 1, 128;" ::: "memory");  // the batch is consumed
+                }
+                if (mode == 1) {
+                    if (etid == 0) {
+                        tc::bulk_wait_all();  // the partial is in global memory ...
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        __threadfence();      // ... before the counter says so
+                        const int prev = atomicAdd(p.counters + t, 1);
+                        *lf = (prev == others) ? 1 : 0;
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (!*lf) break;
+                    mode = 2;  // arrived last after all: reduce (own piece still in TMEM)
+                } else {
+                    if (mode >= 2) {
+                        asm volatile("bar.sync 1, 128;" ::: "memory");
+                        if (etid == 0) p.counters[t] = 0;  // ready for the next launch
+                    }
+                    break;
                 }
             }
             // accumulator drained: the MMA may reuse it
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(accempty0 + 8u * ab);
-            if (!whole) {
-                // stream-K fixup: the last of the tile's pieces to arrive reduces them in K order
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                const long long tb = (long long)t * p.kbpt;
-                const int j0 = cta_of_unit(tb, p.units, G);
-                const int j1 = cta_of_unit(tb + p.kbpt - 1, p.units, G);
-                if (etid == 0) {
-                    const int prev = atomicAdd(p.counters + t, 1);
-                    *last_flag = (prev == j1 - j0) ? 1 : 0;
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (*last_flag) {
-                    __threadfence();
-#pragma unroll 1
-                    for (int c0 = 0; c0 < mvalid; c0 += 16) {
-                        float acc[16];
-#pragma unroll
-                        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
-#pragma unroll 1
-                        for (int j = j0; j <= j1; j += 2) {
-                            // two pieces in flight; summed in piece (= K) order
-                            const int sa_ = (unit_begin(j, p.units, G) >= tb) ? 2 * j : 2 * j + 1;
-                            const float4* pa = reinterpret_cast<const float4*>(
-                                p.ws + ((size_t)sa_ * kTileRows + r) * BN + c0);
-                            float4 va[4], vb[4];
-#pragma unroll
-                            for (int i = 0; i < 4; i++) va[i] = __ldcg(pa + i);
-                            const bool two = j + 1 <= j1;
-                            if (two) {
-                                const int sb_ = (unit_begin(j + 1, p.units, G) >= tb) ? 2 * (j + 1) : 2 * (j + 1) + 1;
-                                const float4* pb = reinterpret_cast<const float4*>(
-                                    p.ws + ((size_t)sb_ * kTileRows + r) * BN + c0);
-#pragma unroll
-                                for (int i = 0; i < 4; i++) vb[i] = __ldcg(pb + i);
-                            }
-#pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                acc[4 * i] += va[i].x;
-                                acc[4 * i + 1] += va[i].y;
-                                acc[4 * i + 2] += va[i].z;
-                                acc[4 * i + 3] += va[i].w;
-                            }
-                            if (two) {
-#pragma unroll
-                                for (int i = 0; i < 4; i++) {
-                                    acc[4 * i] += vb[i].x;
-                                    acc[4 * i + 1] += vb[i].y;
-                                    acc[4 * i + 2] += vb[i].z;
-                                    acc[4 * i + 3] += vb[i].w;
-                                }
-                            }
-                        }
-                        uint32_t d[16];
-#pragma unroll
-                        for (int i = 0; i < 16; i++) d[i] = __float_as_uint(acc[i]);
-                        if (nv)
-                            epi_chunk<OT>(orow + (size_t)c0 * p.N, rrow ? rrow + (size_t)c0 * p.N : nullptr, p.N,
-                                          min(16, mvalid - c0), d, scale, bias, p.bias != nullptr);
-                    }
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
-                    if (etid == 0) p.counters[t] = 0;  // ready for the next launch
-                }
-            }
             seg++;
         }
         if (!ok) raise_error(abort);
+        if (etid == 0) tc::bulk_wait_all();  // outputs written before the dependents may look
         pdl_launch_dependents();
     }
 
@@ -518,62 +652,93 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------- host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn()
+// Weight map: int8 [N, K] in [128 rows x min(BK, 128) B] boxes (128- or 64-byte
+// swizzle); activation map: fp16 [M, K] in [BN rows x 64] boxes, 128-byte
+// swizzled; out-of-range rows/columns read 0.
+bool make_maps(const LinearArgs& a, int BN, int BK, CUtensorMap* mw, CUtensorMap* mx)
 {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-        cudaGetLastError();
-    });
-    return fn;
+    TmapDesc w{};
+    w.base = a.w;
+    w.inner = a.K;
+    w.outer = a.N;
+    w.row_bytes = a.K;
+    w.box_inner = BK < 128 ? (uint32_t)BK : 128u;
+    w.box_outer = kTileRows;
+    w.dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    w.swizzle = w.box_inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    TmapDesc x{};
+    x.base = a.x;
+    x.inner = a.K;
+    x.outer = a.M;
+    x.row_bytes = a.K * 2;
+    x.box_inner = 64;
+    x.box_outer = (uint32_t)BN;
+    x.dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    x.swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+    return tmap_2d(mw, w) && tmap_2d(mx, x);
 }
 
-// Weight map: int8 [N, K] in [128 rows x 128 B] boxes; activation map: fp16 [M, K]
-// in [BN rows x 64] boxes; both 128-byte swizzled, out-of-range rows/columns read 0.
-bool make_maps(const LinearArgs& a, int BN, CUtensorMap* mw, CUtensorMap* mx)
+// Output map: [M, N] fp16 or fp32, row-major, stored in [CH tokens x 128 channels]
+// boxes from an unswizzled staging buffer; out-of-range rows/columns are not written.
+bool make_out_map(const LinearArgs& a, int CH, CUtensorMap* mo)
 {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    const cuuint32_t es[2] = {1, 1};
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.N};
-        const cuuint64_t strides[1] = {(cuuint64_t)a.K};
-        const cuuint32_t box[2] = {128u, (cuuint32_t)kTileRows};
-        if (enc(mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(a.w), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-        const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
-        const cuuint32_t box[2] = {64u, (cuuint32_t)BN};
-        if (enc(mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    return true;
+    TmapDesc o{};
+    o.base = a.out;
+    o.inner = a.N;
+    o.outer = a.M;
+    o.row_bytes = a.N * (a.out_dtype == kF16 ? 2 : 4);
+    o.box_inner = kTileRows;
+    o.box_outer = (uint32_t)CH;
+    o.dtype = a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    o.swizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
+    return tmap_2d(mo, o);
 }
 
-int pick_bn(size_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
-int pick_bk(int BN) { return BN <= 32 ? 256 : 128; }
+// Token-tile width: the smallest UMMA N that covers M up to 128 tokens; above
+// that, 256-token tiles (issue-bound 128-token MMAs run at ~half rate) unless
+// that leaves fewer than a quarter as many tiles as SMs, where the stream-K
+// fixup of the many pieces per tile would cost more than it saves.
+int pick_bn(size_t M, size_t N, int num_sms)
+{
+    if (M <= 16) return 16;
+    if (M <= 32) return 32;
+    if (M <= 64) return 64;
+    if (M <= 128) return 128;
+    const long long tiles256 = (long long)((N + kTileRows - 1) / kTileRows) * (long long)((M + 255) / 256);
+    return 4 * tiles256 >= num_sms ? 256 : 128;
+}
+int pick_bk(int BN) { return BN <= 32 ? 256 : BN <= 128 ? 128 : 64; }
+
+// Grid size: one CTA per SM with stream-K over all units, unless the tiles fit on
+// the SMs whole and finishing each tile in one CTA is quicker than splitting them:
+// a split tile costs its pieces a workspace round trip and a serial fixup (about
+// 12 us plus 1 us per piece, measured), which small problems cannot amortize.
+long long pick_grid(long long tiles, long long kbpt, int BN, int BK, int num_sms)
+{
+    const long long units = tiles * kbpt;
+    const long long sk = units < num_sms ? units : num_sms;
+    if (tiles > num_sms || units % sk == 0 && (units / sk) % kbpt == 0) return sk;  // no split anyway
+    // per-unit time: BK/16 MMAs of max(issue ~70, BN/2) cycles, at ~1.9 GHz, x1.3 for data movement
+    const double unit_us = (BK / 16) * (BN / 2 > 70 ? BN / 2 : 70) / 1900.0 * 1.3;
+    const double dp_us = (double)kbpt * unit_us;
+    const double pieces = (double)sk / (double)tiles + 1.0;
+    const double sk_us = (double)units / (double)sk * unit_us + 12.0 + pieces;
+    return dp_us <= sk_us ? tiles : sk;
+}
 
 template <int BN, int BK, int S, int SA, typename OT>
 cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream)
 {
     using C = SkCfg<BN, BK, S, SA>;
-    CUtensorMap mw, mx;
-    if (!make_maps(a, BN, &mw, &mx)) return cudaErrorInvalidValue;
+    CUtensorMap mw, mx, mo;
+    if (!make_maps(a, BN, BK, &mw, &mx)) return cudaErrorInvalidValue;
+    const size_t ob = a.out_dtype == kF16 ? 2 : 4;
+    const bool tma_out = ((uintptr_t)a.out % 16) == 0 && (a.N * ob) % 16 == 0;
+    if (tma_out) {
+        if (!make_out_map(a, C::kChunk, &mo)) return cudaErrorInvalidValue;
+    } else {
+        mo = mx;  // unused by the kernel
+    }
     auto kern = q8_gemm_sk_kernel<BN, BK, S, SA, OT>;
     static thread_local bool configured[64] = {};
     int dev = 0;
@@ -597,7 +762,8 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
     p.tiles_n = (int)((a.N + kTileRows - 1) / kTileRows);
     const long long tiles = (long long)p.tiles_n * (long long)((a.M + BN - 1) / BN);
     p.units = tiles * p.kbpt;
-    const int G = (int)((p.units < num_sms) ? p.units : num_sms);
+    p.tma_out = tma_out ? 1 : 0;
+    const int G = (int)pick_grid(tiles, p.kbpt, BN, BK, num_sms);
     if ((long long)scratch.ws_floats < 2LL * G * BN * kTileRows || (long long)scratch.counters < tiles)
         return cudaErrorMemoryAllocation;
     p.ws = scratch.ws;
@@ -612,7 +778,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
+    e = cudaLaunchKernelEx(&cfg, kern, mw, mx, mo, p);
     if (e == cudaSuccess) note_launch();
     return e;
 }
@@ -620,11 +786,12 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
 template <typename OT>
 cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream)
 {
-    switch (pick_bn(a.M)) {
+    switch (pick_bn(a.M, a.N, num_sms)) {
         case 16: return launch_cfg<16, 256, 5, 2, OT>(a, num_sms, scratch, stream);
         case 32: return launch_cfg<32, 256, 4, 2, OT>(a, num_sms, scratch, stream);
         case 64: return launch_cfg<64, 128, 6, 3, OT>(a, num_sms, scratch, stream);
-        default: return launch_cfg<128, 128, 4, 3, OT>(a, num_sms, scratch, stream);
+        case 128: return launch_cfg<128, 128, 4, 3, OT>(a, num_sms, scratch, stream);
+        default: return launch_cfg<256, 64, 4, 4, OT>(a, num_sms, scratch, stream);
     }
 }
 
@@ -639,12 +806,11 @@ bool gemm_tc_supports(const LinearArgs& a)
 
 void gemm_tc_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters)
 {
-    const int BN = pick_bn(a.M);
+    const int BN = pick_bn(a.M, a.N, num_sms);
     const int BK = pick_bk(BN);
     const long long tiles_n = (long long)((a.N + kTileRows - 1) / kTileRows);
     const long long tiles = tiles_n * (long long)((a.M + BN - 1) / BN);
-    const long long units = tiles * (long long)((a.K + BK - 1) / BK);
-    const long long G = units < num_sms ? units : num_sms;
+    const long long G = pick_grid(tiles, (long long)((a.K + BK - 1) / BK), BN, BK, num_sms);
     *ws_floats = (size_t)(2 * G * BN * kTileRows);
     *counters = (size_t)tiles;
 }

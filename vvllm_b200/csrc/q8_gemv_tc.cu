@@ -48,6 +48,7 @@
 #include "kernels.h"
 #include "sk_common.cuh"
 #include "tc_utils.cuh"
+#include "tmap.cuh"
 
 namespace b200q8 {
 
@@ -513,37 +514,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------- host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn()
-{
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-        cudaGetLastError();
-    });
-    return fn;
-}
-
 // int8 [rows, K] row-major in [box_rows x 128 B] boxes, 128-byte swizzle, out-of-range reads 0.
 bool make_i8_map(CUtensorMap* m, const void* base, size_t K, size_t rows, int box_rows)
 {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    const cuuint32_t es[2] = {1, 1};
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)K};
-    const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    TmapDesc d{};
+    d.base = base;
+    d.inner = K;
+    d.outer = rows;
+    d.row_bytes = K;
+    d.box_inner = 128;
+    d.box_outer = (uint32_t)box_rows;
+    d.dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    d.swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+    return tmap_2d(m, d);
 }
 
 int pick_nc(size_t M)
