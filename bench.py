@@ -7,8 +7,10 @@ projections -- fused gate/up 3584 -> 37888, down 18944 -> 3584 and lm_head
 3584 -> 152064 -- with fp16 activations, fp32 accumulation and fp16 outputs.
 Weights are synthetic N(0, 0.02), quantized per row by absmax on the GPU;
 activations N(0, 1).  With N GPUs every projection is column-sharded by output
-channel (rank r owns rows [r*N/G, (r+1)*N/G)) and the outputs are all-gathered
-with NCCL, so the total work is fixed as N grows ("strong" scaling).
+channel (rank r owns rows [r*N/G, (r+1)*N/G)) and each rank's GEMV stores its
+slice into every rank's output over NVLink (the gather fused into the kernel;
+the GEMV-then-NCCL-allgather alternative is reported beside it), so the total
+work is fixed as N grows ("strong" scaling).
 
 One step = the three projections once.  `value` is the whole-job algorithmic
 HBM bytes moved per second (int8 weights + fp32 scales + activations in +
@@ -218,42 +220,67 @@ PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 
 
 
 def prefill_tflops(v, dev, stream, warmup: int, iters: int, tc_peak: float):
-    """Config 4: four prefill GEMMs back to back; TFLOP/s of the whole set and per shape."""
+    """Config 4: the four prefill GEMMs (M = 512) back to back, replayed from a CUDA graph
+    (the library's host call costs ~8 us through ctypes, more than the small GEMMs take on the
+    device); L2 flushed before every replay.  Also a Qwen2.5-7B-shaped prefill projection
+    (gate/up, 3584 -> 37888, M = 512) on its own, as the large-shape reference point."""
     import torch
 
     M = 512
     torch.manual_seed(1)
-    cases = []
-    for K, N in PREFILL:
+    stream = torch.cuda.Stream(device=dev)  # graphs are captured on a non-default stream
+    stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def make(K, N):
         q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
         s = torch.rand(N, device=dev) * 1e-3
         x = torch.randn(M, K, device=dev).half()
         out = torch.empty(M, N, device=dev, dtype=torch.float16)
-        cases.append((K, N, q, s, x, out))
+        return (K, N, q, s, x, out)
+
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
-    per = {}
-    total_flop, total_ms = 0.0, 0.0
-    for K, N, q, s, x, out in cases:
+
+    def timed(cases):
+        """Median device time (ms) of one graph replay running `cases` once each."""
         for _ in range(warmup):
-            v.linear_q8(out, x, q, s, stream=stream)
+            for K, N, q, s, x, out in cases:
+                v.linear_q8(out, x, q, s, stream=stream)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for K, N, q, s, x, out in cases:
+                v.linear_q8(out, x, q, s, stream=stream)
         ms = []
-        for _ in range(iters):
-            flush.zero_()  # the GEMM's operands come from HBM, not L2
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            v.linear_q8(out, x, q, s, stream=stream)
-            b.record(stream)
-            b.synchronize()
-            ms.append(a.elapsed_time(b))
-        t = statistics.median(ms)
-        flop = 2.0 * M * N * K
-        per[f"{K}x{N}"] = {"TFLOP/s": round(flop / (t * 1e-3) / 1e12, 1), "us": round(t * 1e3, 2)}
-        total_flop += flop
-        total_ms += t
+        with torch.cuda.stream(stream):
+            for _ in range(iters):
+                flush.zero_()  # the GEMMs' operands come from HBM, not L2
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                g.replay()
+                b.record(stream)
+                b.synchronize()
+                ms.append(a.elapsed_time(b))
+        del g
+        return statistics.median(ms)
+
+    cases = [make(K, N) for K, N in PREFILL]
+    per = {}
+    for c in cases:
+        t = timed([c])
+        flop = 2.0 * M * c[1] * c[0]
+        per[f"{c[0]}x{c[1]}"] = {"TFLOP/s": round(flop / (t * 1e-3) / 1e12, 1), "us": round(t * 1e3, 2)}
+    total_flop = sum(2.0 * M * N * K for K, N, *_ in cases)
+    total_ms = timed(cases)
     value = total_flop / (total_ms * 1e-3) / 1e12
+    big = make(HIDDEN, 2 * INTER)
+    t_big = timed([big])
+    f_big = 2.0 * M * big[1] * big[0]
+    v_big = f_big / (t_big * 1e-3) / 1e12
     return {"value": round(value, 1), "unit": "TFLOP/s", "frac": round(value / tc_peak, 4),
-            "peak": tc_peak, "M": M, "per_shape": per,
-            "timing": "median single launch per shape, L2 flushed before each, host launch cost included"}
+            "peak": tc_peak, "M": M, "per_shape": per, "set_us": round(total_ms * 1e3, 2),
+            "gate_up_7b_M512": {"TFLOP/s": round(v_big, 1), "frac": round(v_big / tc_peak, 4),
+                                "us": round(t_big * 1e3, 2)},
+            "timing": "median CUDA-graph replay (device time), L2 flushed before each replay"}
 
 
 def profile_case(args):
