@@ -338,3 +338,26 @@ def test_full_size_sampled_rows(cuda, oracle, name, N, K, M):
     ref = oracle.linear_q8(x.float().cpu().numpy(), q_rows, s_rows, None)
     y = out[:, rows].float().cpu().numpy()
     assert rowwise_normwise_err(y, ref) <= TOL_F16
+
+
+@pytest.mark.parametrize("M", [1, 3, 6])
+def test_i8_fp16_x_8byte_aligned(cuda, oracle, M):
+    """fp16 activations only 8-byte aligned (a view 4 halves into a buffer) on the digit GEMV,
+    with the in-kernel exponents (M <= 4) and with the prep kernel (M > 4)."""
+    import torch
+
+    import vvllm_b200 as v
+
+    N, K = 640, 896
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 61))
+    x = make_x(M, K, 62)
+    xb = torch.zeros(M * K + 8, dtype=torch.float16, device=cuda)
+    xv = xb[4:4 + M * K].view(M, K)
+    xv.copy_(torch.from_numpy(x).to(cuda).half())
+    assert xv.data_ptr() % 16 == 8
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    v.linear_q8_ex(out, xv, torch.from_numpy(q).to(cuda), torch.from_numpy(s).to(cuda), algo=v.ALGO_TC_I8)
+    torch.cuda.synchronize()
+    assert v.kernel_error() == 0
+    ref = oracle.linear_q8(xv.float().cpu().numpy(), q, s, None)
+    assert rowwise_normwise_err(out.float().cpu().numpy(), ref) <= TOL_F16

@@ -64,6 +64,10 @@ constexpr int kDigits = 6;
 constexpr int kF16Exp = 24;  // 2^24 * fp16 is an integer for every finite fp16
 constexpr int kQBits = 40;   // |x_q| < 2^40
 constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
+// Up to this many tokens of at most this length, every CTA scans x for the exponents itself
+// (saves the prep kernel's launch); longer rows would delay the first digits more than that.
+constexpr int kFusedExpTokens = 4;
+constexpr size_t kFusedExpMaxK = 4096;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 
 struct DigParams {
@@ -79,6 +83,7 @@ struct DigParams {
     int kbpt;
     long long units;
     P2POut po;        // output placement: local only (ndst = 1) or every rank's copy
+    int fused_exps;   // exponents computed in-kernel (few tokens) instead of by the prep kernel
 };
 
 template <int NC, int BK, int S>
@@ -92,7 +97,7 @@ struct DigCfg {
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                      : kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kNumBars = 3 * S + 4 + 1;  // full, dfull, empty per stage; acc x4; drain
-    static constexpr int kSmemBytes = 1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16;
+    static constexpr int kSmemBytes = 1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 32;
     static_assert(NC % 16 == 0 && NC >= 16 && NC <= 256, "kind::i8 N for M=128");
     static_assert(BK % 128 == 0, "whole 128-byte boxes");
     static_assert(kColsNeeded <= 512, "TMEM overflow");
@@ -122,12 +127,13 @@ __global__ void __launch_bounds__(1024) exps_kernel(const XT* __restrict__ x, in
     float mx = 0.0f;
     int bad = 0;
     if (sizeof(XT) == 2) {
-        const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x) + (size_t)m * K);
-        for (int i = threadIdx.x; i < (K >> 3); i += blockDim.x) {
-            const uint4 v = xr[i];
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        // 8-byte loads: fp16 activations are only required to be 8-byte aligned
+        const uint2* xr = reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(x) + (size_t)m * K);
+        for (int i = threadIdx.x; i < (K >> 2); i += blockDim.x) {
+            const uint2 v = xr[i];
+            const uint32_t w[2] = {v.x, v.y};
 #pragma unroll
-            for (int j = 0; j < 4; j++)  // exponent field all ones: Inf or NaN
+            for (int j = 0; j < 2; j++)  // exponent field all ones: Inf or NaN
                 if (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) bad = 1;
         }
     } else {
@@ -200,7 +206,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sD + S * C::kDBytes);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]
+    int* s_exps = reinterpret_cast<int*>(tmem_holder + 4);                          // [kMaxTokens]
+    float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [8] exponent reduction
 
     const uint32_t bar0 = tc::smem_u32(bars);
     const uint32_t full0 = bar0, dfull0 = bar0 + 8u * S, empty0 = bar0 + 16u * S, accfull0 = bar0 + 24u * S,
@@ -326,7 +334,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= kFirstDig) {
         // ------------------------------------------------------------ digitizers
         const int dtid = threadIdx.x - kFirstDig * 32;  // 0..127
-        pdl_wait();  // x and the prep kernel's exponents are ready
+        pdl_wait();  // x (and the prep kernel's exponents) are ready
+        if (p.fused_exps) {
+            // Few tokens: every CTA finds the per-token exponents itself (the prep kernel's
+            // rule: fp16 e = 24; fp32 e = 39 - floor(log2 max|x|); INT_MIN if any Inf/NaN).
+            const int wd = dtid >> 5;
+#pragma unroll 1
+            for (int m = 0; m < p.M; m++) {
+                float mx = 0.0f;
+                int bad = 0;
+                if (sizeof(XT) == 2) {
+                    // 8-byte loads: fp16 activations need only 8-byte alignment on this path
+                    const uint2* xr = reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.x) + (size_t)m * p.K);
+                    for (int i = dtid; i < (p.K >> 2); i += 128) {
+                        const uint2 v = xr[i];
+                        const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+                        for (int j = 0; j < 2; j++)  // exponent field all ones: Inf or NaN
+                            bad |= (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) ? 1 : 0;
+                    }
+                } else {
+                    const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (size_t)m * p.K);
+                    for (int i = dtid; i < (p.K >> 2); i += 128) {
+                        const float4 v = xr[i];
+                        const float a[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {  // NaN and Inf fail a <= FLT_MAX
+                            bad |= (a[j] <= FLT_MAX) ? 0 : 1;
+                            mx = (a[j] <= FLT_MAX) ? fmaxf(mx, a[j]) : mx;
+                        }
+                    }
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+                }
+                if (lane == 0) {
+                    s_red[wd] = mx;
+                    s_red[4 + wd] = __int_as_float(bad);
+                }
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                if (dtid == 0) {
+                    float m_all = 0.0f;
+                    int b_all = 0;
+                    for (int i = 0; i < 4; i++) {
+                        m_all = fmaxf(m_all, s_red[i]);
+                        b_all |= __float_as_int(s_red[4 + i]);
+                    }
+                    int e;
+                    if (b_all) e = INT_MIN;
+                    else if (sizeof(XT) == 2) e = kF16Exp;
+                    else e = (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
+                    s_exps[m] = e;
+                }
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+            }
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents ready for the epilogue
+        }
+        const int* exps = p.fused_exps ? s_exps : p.exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
         sk::SegIter it(u_begin, u_end, p.kbpt);
@@ -345,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int m = item / (BK / 4);
                     const int kk = (item - m * (BK / 4)) * 4;  // 0..BK-4
                     const int k = kb * BK + kk;
-                    const int e = p.exps[m];
+                    const int e = exps[m];
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
                     if (k < p.K && e != INT_MIN) {
                         float v[4];
@@ -379,6 +444,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue
         pdl_wait();  // exps come from the prep kernel
+        // the per-token exponents, once per CTA (they are read for every output)
+        if (p.fused_exps) {
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // computed by the digitizers
+        } else {
+            if (threadIdx.x - kFirstEpi * 32 < p.M) s_exps[threadIdx.x - kFirstEpi * 32] = p.exps[threadIdx.x - kFirstEpi * 32];
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
@@ -392,91 +464,136 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ncols = kDigits * p.M;
         while (it.next(t, k0, k1)) {
             const int ab = seg & 1, use = seg >> 1;
-            ok = __all_sync(0xffffffffu,
-                            tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
-            if (!ok) break;
-            tc::tc_fence_after();
+            // the row's scale and bias load while the accumulator fills
             const int n = t * kTileRows + r;
             const bool nv = n < p.N;
             const float scale = nv ? p.scales[n] : 0.0f;
             const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
+            ok = __all_sync(0xffffffffu,
+                            tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            if (!ok) break;
+            tc::tc_fence_after();
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
             const bool whole = (k0 == 0 && k1 == p.kbpt);
+            const long long tb = (long long)t * p.kbpt;
+            const int j0 = whole ? cta : sk::cta_of_unit(tb, p.units, G);
+            const int j1 = whole ? cta : sk::cta_of_unit(tb + p.kbpt - 1, p.units, G);
+            volatile int* lf = last_flag + (seg == 0 ? 0 : 1);
+            bool last = whole;
+            if (!whole) {
+                // A piece that finds every other piece already in is the last one: it reduces
+                // with its own digit sums taken straight from TMEM, skipping its own round trip.
+                if (etid == 0) {
+                    int seen;
+                    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(p.counters + t) : "memory");
+                    *lf = (seen == j1 - j0) ? 1 : 0;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                last = *lf != 0;
+            }
             const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
             int* wrow = p.ws + ((size_t)slot * kTileRows + r) * NC;
-            // Each token's six digit sums sit in consecutive TMEM columns; take 8 tokens
-            // (48 columns, three 16-column loads) at a time.
+            // Each token's six digit sums sit in consecutive TMEM columns; take kGT tokens (kGC
+            // columns, 16-column loads) at a time.  A non-last piece stores them to its
+            // workspace slot; the last piece adds every other piece's sums (all loads in flight)
+            // and writes the outputs.
+            constexpr int kGT = NC >= 48 ? 8 : NC / kDigits;     // tokens per group
+            constexpr int kGC = (kGT * kDigits + 15) / 16 * 16;  // TMEM columns per group
 #pragma unroll 1
-            for (int mg = 0; mg < p.M; mg += 8) {
-                const int base = mg * kDigits;
-                int dreg[48];
+            for (int pass = 0; pass < 2; pass++) {
+#pragma unroll 1
+                for (int mg = 0; mg < p.M; mg += kGT) {
+                    const int base = mg * kDigits;
+                    int dreg[kGC];
 #pragma unroll
-                for (int c = 0; c < 48; c += 16) {
-                    if (base + c < ncols) {
-                        uint32_t d[16];
-                        __syncwarp();
-                        tc::tmem_ld_32x32b_x16(d_tmem + base + c, d);
-                        tc::tmem_ld_wait();
+                    for (int c = 0; c < kGC; c += 16) {
+                        if (base + c < ncols) {
+                            uint32_t d[16];
+                            __syncwarp();
+                            tc::tmem_ld_32x32b_x16(d_tmem + base + c, d);
+                            tc::tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 16; i++) dreg[c + i] = (int)d[i];
-                    } else {
+                            for (int i = 0; i < 16; i++) dreg[c + i] = (int)d[i];
+                        } else {
 #pragma unroll
-                        for (int i = 0; i < 16; i++) dreg[c + i] = 0;
-                    }
-                }
-                if (whole) {
-                    if (nv) {
-#pragma unroll
-                        for (int tt = 0; tt < 8; tt++) {
-                            const int m = mg + tt;
-                            if (m < p.M) {
-                                long long ds[kDigits];
-#pragma unroll
-                                for (int i = 0; i < kDigits; i++) ds[i] = dreg[tt * kDigits + i];
-                                epi_out<OT>(p, m, n, recombine(ds, p.exps[m]), scale, bias, has_bias);
-                            }
+                            for (int i = 0; i < 16; i++) dreg[c + i] = 0;
                         }
                     }
-                } else {
+                    if (!last) {
 #pragma unroll
-                    for (int c = 0; c < 48; c += 4)
-                        if (base + c < ncols)
-                            __stcg(reinterpret_cast<int4*>(wrow + base + c),
-                                   make_int4(dreg[c], dreg[c + 1], dreg[c + 2], dreg[c + 3]));
+                        for (int c = 0; c < kGC; c += 4)
+                            if (base + c < ncols)
+                                __stcg(reinterpret_cast<int4*>(wrow + base + c),
+                                       make_int4(dreg[c], dreg[c + 1], dreg[c + 2], dreg[c + 3]));
+                        continue;
+                    }
+                    const int mend = min(kGT, p.M - mg);
+#pragma unroll 1
+                    for (int tt = 0; tt < mend; tt++) {
+                        const int m = mg + tt;
+                        long long ds[kDigits];
+#pragma unroll
+                        for (int i = 0; i < kDigits; i++) ds[i] = 0;
+                        // this CTA's own sums (dreg is indexed with a run-time token: select by tt)
+#pragma unroll
+                        for (int u = 0; u < kGT; u++)
+                            if (u == tt) {
+#pragma unroll
+                                for (int i = 0; i < kDigits; i++) ds[i] = dreg[u * kDigits + i];
+                            }
+                        // the other pieces, kPB at a time with all their loads in flight (more
+                        // would spill registers)
+                        constexpr int kPB = 4;
+#pragma unroll 1
+                        for (int j = j0; j <= j1; j += kPB) {
+                            int vv[kPB][kDigits];
+#pragma unroll
+                            for (int u = 0; u < kPB; u++) {
+                                const int jj = j + u;
+                                if (jj <= j1 && jj != cta) {
+                                    const int2* pj = reinterpret_cast<const int2*>(
+                                        p.ws + ((size_t)sk::piece_slot(jj, tb, p.units, G) * kTileRows + r) * NC + m * kDigits);
+#pragma unroll
+                                    for (int i = 0; i < kDigits / 2; i++) {
+                                        const int2 w = __ldcg(pj + i);
+                                        vv[u][2 * i] = w.x;
+                                        vv[u][2 * i + 1] = w.y;
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int i = 0; i < kDigits; i++) vv[u][i] = 0;
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < kPB; u++)
+#pragma unroll
+                                for (int i = 0; i < kDigits; i++) ds[i] += vv[u][i];
+                        }
+                        if (nv) epi_out<OT>(p, m, n, recombine(ds, s_exps[m]), scale, bias, has_bias);
+                    }
                 }
+                if (last) {
+                    if (!whole) {
+                        asm volatile("bar.sync 1, 128;" ::: "memory");
+                        if (etid == 0) p.counters[t] = 0;  // ready for the next launch
+                    }
+                    break;
+                }
+                // this piece's sums are out: count it in; the last one to arrive reduces
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (etid == 0) {
+                    const int prev = atomicAdd(p.counters + t, 1);
+                    *lf = (prev == j1 - j0) ? 1 : 0;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (!*lf) break;
+                last = true;
+                __threadfence();  // acquire: the other pieces' sums
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(accempty0 + 8u * ab);  // accumulator drained
-            if (!whole) {
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                const long long tb = (long long)t * p.kbpt;
-                const int j0 = sk::cta_of_unit(tb, p.units, G);
-                const int j1 = sk::cta_of_unit(tb + p.kbpt - 1, p.units, G);
-                if (etid == 0) {
-                    const int prev = atomicAdd(p.counters + t, 1);
-                    *last_flag = (prev == j1 - j0) ? 1 : 0;
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (*last_flag) {
-                    __threadfence();
-#pragma unroll 1
-                    for (int m = 0; m < p.M; m++) {
-                        long long ds[kDigits] = {0, 0, 0, 0, 0, 0};
-#pragma unroll 1
-                        for (int j = j0; j <= j1; j++) {
-                            const int* pj = p.ws + ((size_t)sk::piece_slot(j, tb, p.units, G) * kTileRows + r) * NC +
-                                            m * kDigits;
-#pragma unroll
-                            for (int i = 0; i < kDigits; i++) ds[i] += __ldcg(pj + i);
-                        }
-                        if (nv) epi_out<OT>(p, m, n, recombine(ds, p.exps[m]), scale, bias, has_bias);
-                    }
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
-                    if (etid == 0) p.counters[t] = 0;
-                }
-            }
             seg++;
         }
         if (!ok) raise_error(abort);
@@ -578,6 +695,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.res = a.res;
     p.out = a.out;
     p.exps = sc.exps;
+    p.fused_exps = (a.M <= kFusedExpTokens && a.K <= kFusedExpMaxK) ? 1 : 0;
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -599,6 +717,8 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
         sc.exps_count < a.M)
         return cudaErrorMemoryAllocation;
+    if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
+        return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M), dim3(1024), 0, stream, a.pdl,
                   reinterpret_cast<const XT*>(a.x), (int)a.K, sc.exps);
     if (e != cudaSuccess) return e;
