@@ -400,7 +400,10 @@ def main():
             if ev is not None and i == lm_idx:
                 ev[0].record(stream)
             if comm is not None and mode == "p2p":
-                v.linear_q8_sharded_p2p(comm, p2p_outs[i], xs[i], q, s, None, N, stream=stream)
+                # each call's completion wait is paid by the next gathered call (inside its GEMV
+                # when it can) or by the Comm.wait() that ends the timed region
+                v.linear_q8_sharded_p2p(comm, p2p_outs[i], xs[i], q, s, None, N, stream=stream,
+                                        defer_wait=True)
             else:
                 slot = outs[i][:, rank * per[i]: rank * per[i] + rows]
                 v.linear_q8(slot, xs[i], q, s, None, stream=stream)
@@ -416,6 +419,8 @@ def main():
 
     for it in range(args.warmup):
         step(it)
+    if comm is not None:
+        comm.wait(stream)
     barrier()
 
     lm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -428,6 +433,8 @@ def main():
         t_start.record(stream)
         for it in range(args.steps):
             step(it, lm_events[it])
+        if comm is not None:
+            comm.wait(stream)
         t_end.record(stream)
         barrier()
         n_launch = v.launch_count() - n0
@@ -501,7 +508,10 @@ def main():
             if comm is None:
                 v.linear_q8(d_outs[i], d_in[i], q, s, None, stream=stream)
             else:
-                v.linear_q8_sharded_p2p(comm, d_outs[i], d_in[i], q, s, None, N, stream=stream)
+                v.linear_q8_sharded_p2p(comm, d_outs[i], d_in[i], q, s, None, N, stream=stream,
+                                        defer_wait=True)
+        if comm is not None:
+            comm.wait(stream)  # every gathered output complete before the copy out
         h_out.copy_(out_src, non_blocking=True)
 
     for it in range(args.warmup):
@@ -533,10 +543,16 @@ def main():
         shapes = host_sample_weights(args.cpu_sample)
         gbs, sec, iters = time_cpu_linear(lib, shapes, cores, args.cpu_budget)
         sb = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
+        # the reference runs single-threaded: time that too, on a smaller row sample
+        shapes1 = host_sample_weights(args.cpu_sample / 8, seed=1)
+        gbs1, sec1, iters1 = time_cpu_linear(lib, shapes1, 1, args.cpu_budget / 2)
         cpu_baseline = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
                         "sample": f"{args.cpu_sample:.3f} of each projection's rows "
                                   f"({sb / 1e6:.1f} MB algorithmic), {iters} passes in {sec * iters:.1f} s, "
-                                  f"{cores} threads; CPU: {model}"}
+                                  f"{cores} threads (disjoint output-row slices); CPU: {model}",
+                        "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                          "sample": f"{args.cpu_sample / 8:.4f} of each projection's rows, "
+                                                    f"{iters1} passes in {sec1 * iters1:.1f} s"}}
 
     if rank == 0:
         traffic = profiled_traffic("q8_gemv_dig_lm_head_7b") if world == 1 else None

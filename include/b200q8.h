@@ -217,6 +217,20 @@ B200Q8_API int b200q8_linear_q8_sharded_p2p(b200q8_comm* comm, void* out, int ou
                                             const float* bias_shard, size_t M, size_t N, size_t K,
                                             b200q8_stream_t stream);
 
+/* As b200q8_linear_q8_sharded_p2p, with B200Q8_P2P_DEFER_WAIT in `flags`: the call enqueues no
+ * wait, so `out` is NOT yet complete in stream order.  The wait is owed by the communicator and
+ * paid by its next gathered call (inside that call's GEMV when it has few short tokens, M <= 4
+ * and K <= 4096, else as a wait kernel ahead of it) or by b200q8_comm_wait.  Any other consumer
+ * of `out` must come after b200q8_comm_wait on the same stream.  Chains of deferred calls must
+ * stay on one stream. */
+#define B200Q8_P2P_DEFER_WAIT 1u
+B200Q8_API int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
+                                               int in_dtype, const int8_t* w_shard, const float* scales_shard,
+                                               const float* bias_shard, size_t M, size_t N, size_t K,
+                                               unsigned int flags, b200q8_stream_t stream);
+/* Enqueues the wait a deferred gathered call still owes (no-op when none is owed). */
+B200Q8_API int b200q8_comm_wait(b200q8_comm* comm, b200q8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,9 @@ _SIGS = {
     "b200q8_comm_sym_free": ([_vp, _vp], _int),
     "b200q8_linear_q8_sharded_p2p": (
         [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_linear_q8_sharded_p2p_ex": (
+        [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, ctypes.c_uint, _vp], _int),
+    "b200q8_comm_wait": ([_vp, _vp], _int),
 }
 
 # Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
@@ -259,6 +262,10 @@ class Comm:
     def sym_free(self, t) -> None:
         _check(lib().b200q8_comm_sym_free(self.h, _addr(t)))
 
+    def wait(self, stream=None) -> None:
+        """Enqueue the completion wait a deferred gathered call still owes (no-op if none)."""
+        _check(lib().b200q8_comm_wait(self.h, _stream(stream)))
+
     def abort(self) -> None:
         if self.h:
             h, self.h = self.h, None
@@ -275,11 +282,16 @@ def linear_q8_sharded(comm: Comm, out, x, w_shard, scales_shard, bias_shard, N: 
                                           _stream(stream)))
 
 
+P2P_DEFER_WAIT = 1
+
+
 def linear_q8_sharded_p2p(comm: Comm, out, x, w_shard, scales_shard, bias_shard, N: int,
-                          stream=None) -> None:
+                          stream=None, defer_wait: bool = False) -> None:
     """out[M,N] (all ranks) = linear_q8 over the column-sharded weight; the GEMV stores every
-    rank's slice into every rank's `out` over NVLink.  `out` lies in a Comm.sym_alloc tensor."""
+    rank's slice into every rank's `out` over NVLink.  `out` lies in a Comm.sym_alloc tensor.
+    defer_wait: leave the completion wait to the next gathered call or Comm.wait()."""
     M, K = x.shape
-    _check(lib().b200q8_linear_q8_sharded_p2p(comm.h, _addr(out), _dtype_code(out), _addr(x),
-                                              _dtype_code(x), _addr(w_shard), _addr(scales_shard),
-                                              _addr(bias_shard), M, N, K, _stream(stream)))
+    _check(lib().b200q8_linear_q8_sharded_p2p_ex(comm.h, _addr(out), _dtype_code(out), _addr(x),
+                                                 _dtype_code(x), _addr(w_shard), _addr(scales_shard),
+                                                 _addr(bias_shard), M, N, K,
+                                                 P2P_DEFER_WAIT if defer_wait else 0, _stream(stream)))

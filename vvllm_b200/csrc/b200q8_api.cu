@@ -664,9 +664,9 @@ struct b200q8_comm {
     double timeout_s = 60.0;
     cudaStream_t xstream = nullptr;  // internal stream for handle exchanges
     std::vector<SymAlloc> syms;
-    SymAlloc flags;                  // unsigned flags[nranks] per rank, written by the peers
-    unsigned int* done_ctr = nullptr;
+    SymAlloc flags;                  // u64 counts[nranks] per rank, advanced by the peers' GEMVs
     unsigned int seq = 0;            // calls of the in-kernel gather so far (identical on all ranks)
+    unsigned int pending = 0;        // seq of a deferred call whose wait is still owed (0: none)
 };
 
 namespace {
@@ -773,8 +773,6 @@ void comm_release(b200q8_comm* c)
     for (auto& s : c->syms) sym_close(c, &s);
     c->syms.clear();
     if (c->flags.local) sym_close(c, &c->flags);
-    if (c->done_ctr) cudaFree(c->done_ctr);
-    c->done_ctr = nullptr;
     if (c->xstream) cudaStreamDestroy(c->xstream);
     c->xstream = nullptr;
 }
@@ -906,14 +904,15 @@ int b200q8_comm_destroy(b200q8_comm* c)
     return rc;
 }
 
-int b200q8_linear_q8_sharded_p2p(b200q8_comm* c, void* out, int out_dtype, const void* inp, int in_dtype,
-                                 const int8_t* w_shard, const float* scales_shard, const float* bias_shard,
-                                 size_t M, size_t N, size_t K, b200q8_stream_t stream)
+int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, const void* inp, int in_dtype,
+                                    const int8_t* w_shard, const float* scales_shard, const float* bias_shard,
+                                    size_t M, size_t N, size_t K, unsigned int flags, b200q8_stream_t stream)
 {
     if (!c) return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: null comm");
     if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
         return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: bad dtype");
-    if (M == 0 || N == 0) return B200Q8_OK;
+    if (flags & ~(unsigned)B200Q8_P2P_DEFER_WAIT) return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: bad flags");
+    if (M == 0 || N == 0) return b200q8_comm_wait(c, stream);
     if (!out || !inp || !w_shard || !scales_shard)
         return fail(B200Q8_ERR_INVALID, "linear_q8_sharded_p2p: null pointer");
     const int G = c->nranks;
@@ -935,22 +934,19 @@ int b200q8_linear_q8_sharded_p2p(b200q8_comm* c, void* out, int out_dtype, const
                     "linear_q8_sharded_p2p: out must lie in a buffer from b200q8_comm_sym_alloc on this communicator");
     if ((st = set_device(c->device))) return st;
     cudaError_t e;
-    if (!c->flags.local) {  // first call: the flags every peer writes into (collective)
+    if (!c->flags.local) {  // first call: the completion counts every peer adds to (collective)
         if ((st = sym_open(c, 256, &c->flags))) return st;
-        if ((e = cudaMalloc(&c->done_ctr, sizeof(unsigned int))) != cudaSuccess ||
-            (e = cudaMemset(c->done_ctr, 0, sizeof(unsigned int))) != cudaSuccess)
-            return cuda_fail(e, "linear_q8_sharded_p2p: counter");
     }
     const size_t off = (uintptr_t)out - (uintptr_t)sym->local;
     P2POut po;
     po.ndst = G;
     for (int j = 0; j < G; j++) {
         po.dst[j] = (char*)sym->peer[j] + off;
-        po.flags[j] = reinterpret_cast<unsigned int*>(c->flags.peer[j]);
+        po.counts[j] = reinterpret_cast<unsigned long long*>(c->flags.peer[j]);
     }
     po.ldo = (long long)N;
     po.ocol0 = (int)row0;
-    po.done_ctr = c->done_ctr;
+    po.publish = 1;
     po.rank = c->rank;
     po.seq = ++c->seq;
     DeviceInfo d;
@@ -975,13 +971,52 @@ int b200q8_linear_q8_sharded_p2p(b200q8_comm* c, void* out, int out_dtype, const
     gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
     TcScratch scratch;
     if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
+    // A deferred wait of the previous call is owed before this call reads its input: inside the
+    // GEMV when it reads x only in-kernel, else as the wait kernel ahead of it.
+    if (c->pending) {
+        if (gemv_i8_fused_exps(a)) {
+            po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
+            po.wait_n = G;
+            po.wait_seq = c->pending;
+            c->pending = 0;
+        } else if ((st = b200q8_comm_wait(c, stream))) {
+            return st;
+        }
+    }
     if ((e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream)) != cudaSuccess)
         return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");
-    if ((e = launch_p2p_wait(reinterpret_cast<unsigned int*>(c->flags.local), G, c->rank, po.seq,
+    if (flags & B200Q8_P2P_DEFER_WAIT) {
+        c->pending = po.seq;  // the next gathered call (or b200q8_comm_wait) waits for it
+        return B200Q8_OK;
+    }
+    if ((e = launch_p2p_wait(reinterpret_cast<const unsigned long long*>(c->flags.local), G, c->rank, po.seq,
                              2000000000ull, (cudaStream_t)stream)) != cudaSuccess)
         return cuda_fail(e, "linear_q8_sharded_p2p: wait launch");
     return B200Q8_OK;
 }
+
+int b200q8_linear_q8_sharded_p2p(b200q8_comm* c, void* out, int out_dtype, const void* inp, int in_dtype,
+                                 const int8_t* w_shard, const float* scales_shard, const float* bias_shard,
+                                 size_t M, size_t N, size_t K, b200q8_stream_t stream)
+{
+    return b200q8_linear_q8_sharded_p2p_ex(c, out, out_dtype, inp, in_dtype, w_shard, scales_shard, bias_shard,
+                                           M, N, K, 0u, stream);
+}
+
+int b200q8_comm_wait(b200q8_comm* c, b200q8_stream_t stream)
+{
+    if (!c) return fail(B200Q8_ERR_INVALID, "comm_wait: null comm");
+    if (!c->pending) return B200Q8_OK;
+    int st = set_device(c->device);
+    if (st) return st;
+    cudaError_t e = launch_p2p_wait(reinterpret_cast<const unsigned long long*>(c->flags.local), c->nranks, c->rank,
+                                    c->pending, 2000000000ull, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "comm_wait: wait launch");
+    c->pending = 0;
+    return B200Q8_OK;
+}
+
+
 
 int b200q8_comm_allgather(b200q8_comm* c, void* buf, size_t count, int dtype, b200q8_stream_t stream)
 {

@@ -16,25 +16,25 @@ __device__ int g_kernel_error_p2p;  // bit 1: a peer's flag did not arrive in ti
 
 namespace {
 
-// flags[j] is written (system-scope release) by rank j's GEMV when its output
-// slice has landed in this rank's output; a peer can run at most one call
-// ahead, so "arrived" is seq' - seq >= 0 in wrapping arithmetic.  The kernel
-// is launched as a programmatic dependent of this rank's GEMV and lets its own
-// dependents launch at once: they only pass griddepcontrol.wait once every
-// rank's flag, this rank's included, has been seen here.
-__global__ void p2p_wait_kernel(const unsigned int* flags, int nranks, int rank, unsigned int seq,
+// counts[j] grows by 2^kCountShift per call of rank j once all of that call's CTAs have
+// stored their outputs here (system-scope release reductions); a peer can run at most one
+// call ahead, so "arrived" is a wrapping compare.  The kernel is launched as a programmatic
+// dependent of this rank's GEMV and lets its own dependents launch at once: they only pass
+// griddepcontrol.wait once every rank's count, this rank's included, has been seen here.
+__global__ void p2p_wait_kernel(const unsigned long long* counts, int nranks, int rank, unsigned int seq,
                                 unsigned long long timeout_ns)
 {
     pdl_launch_dependents();
     if (threadIdx.x != 0) return;
+    const unsigned long long target = (unsigned long long)seq << kCountShift;
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     for (int i = 1; i <= nranks; i++) {
-        const int j = (rank + i) % nranks;  // own flag last (written last by the local GEMV)
+        const int j = (rank + i) % nranks;
         for (;;) {
-            unsigned int v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + j) : "memory");
-            if ((int)(v - seq) >= 0) break;
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counts + j) : "memory");
+            if ((long long)(v - target) >= 0) break;
             unsigned long long t;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
             if (t - t0 > timeout_ns) {
@@ -79,7 +79,7 @@ cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, si
     return e;
 }
 
-cudaError_t launch_p2p_wait(const unsigned int* flags, int nranks, int rank, unsigned int seq,
+cudaError_t launch_p2p_wait(const unsigned long long* counts, int nranks, int rank, unsigned int seq,
                             unsigned long long timeout_ns, cudaStream_t stream)
 {
     cudaLaunchConfig_t cfg = {};
@@ -91,7 +91,7 @@ cudaError_t launch_p2p_wait(const unsigned int* flags, int nranks, int rank, uns
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_wait_kernel, flags, nranks, rank, seq, timeout_ns);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_wait_kernel, counts, nranks, rank, seq, timeout_ns);
     if (e == cudaSuccess) note_launch();
     return e;
 }

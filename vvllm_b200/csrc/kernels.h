@@ -12,18 +12,27 @@ enum DType : int { kF32 = 0, kF16 = 1 };
 // Output placement for the column-sharded path with an in-kernel gather: every
 // output element is stored into `ndst` copies of the full [M, ldo] output
 // (the local one and each peer's, mapped over NVLink), at column ocol0 + row.
-// When the last CTA of the launch is done it writes `seq` into flags[rank] of
-// every rank (system-scope release); peers wait for it before reading.
+// Completion: when a CTA is done it adds its share of 2^20 to counts[rank] on
+// every rank (system-scope release reduction; CTA 0 adds 2^20 - (grid - 1), the
+// others 1), so counts[j] on a rank reaches seq * 2^20 once all of rank j's CTAs of
+// call `seq` have stored their outputs there.
 constexpr int kMaxRanks = 8;
+constexpr int kCountShift = 20;  // each call adds 2^20 to every rank's count slot
 struct P2POut {
     int ndst = 1;
     void* dst[kMaxRanks] = {};
     long long ldo = 0;
     int ocol0 = 0;
-    unsigned int* done_ctr = nullptr;          // local, zero between launches
-    unsigned int* flags[kMaxRanks] = {};        // flags array base on every rank
+    int publish = 0;                             // add this launch's completion shares
+    unsigned long long* counts[kMaxRanks] = {};  // count array base on every rank
     int rank = 0;
     unsigned int seq = 0;
+    // Deferred wait of the previous gathered call: before x (or a residual) is read, every
+    // rank's count in wait_counts[0..wait_n) must have reached wait_seq << kCountShift
+    // (wait_seq 0: nothing to wait for).
+    const unsigned long long* wait_counts = nullptr;
+    int wait_n = 0;
+    unsigned int wait_seq = 0;
 };
 
 struct LinearArgs {
@@ -39,9 +48,9 @@ struct LinearArgs {
     const P2POut* p2p = nullptr;    // int8 digit GEMV only: gather into peers' outputs
 };
 
-// One thread waits (bounded, `timeout_ns`) until flags[j] == seq for every rank j != rank;
-// on expiry it sets bit 1 of the device error word and returns.
-cudaError_t launch_p2p_wait(const unsigned int* flags, int nranks, int rank, unsigned int seq,
+// One thread waits (bounded, `timeout_ns`) until counts[j] has reached seq << kCountShift for
+// every rank j; on expiry it sets bit 1 of the device error word and returns.
+cudaError_t launch_p2p_wait(const unsigned long long* counts, int nranks, int rank, unsigned int seq,
                             unsigned long long timeout_ns, cudaStream_t stream);
 cudaError_t read_kernel_error_p2p(int* code, bool clear);
 
@@ -73,6 +82,9 @@ struct TcScratch {
 // activations (fp16 or fp32 inputs) and kind::i8 MMAs on the raw int8 weights.
 cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream);
 bool gemv_i8_supports(const LinearArgs& a);
+// True when the GEMV computes the per-token exponents itself (one launch, x read only in-kernel,
+// so a deferred peer wait can happen inside it).
+bool gemv_i8_fused_exps(const LinearArgs& a);
 int gemv_i8_max_tokens();
 void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* dig_bytes,
                           size_t* exps);

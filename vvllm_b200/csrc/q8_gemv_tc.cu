@@ -42,6 +42,7 @@
 #include <limits.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -69,6 +70,7 @@ constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
 constexpr int kFusedExpTokens = 4;
 constexpr size_t kFusedExpMaxK = 4096;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
+constexpr uint64_t kPeerTimeoutNs = 2000000000ull;  // a peer's flag of the previous gathered call
 
 struct DigParams {
     const void* x;    // [M, K] fp16 or fp32
@@ -109,6 +111,24 @@ __device__ __forceinline__ void raise_error(volatile int* abort)
 {
     *abort = 1;
     atomicOr(&g_kernel_error_i8, 1);
+}
+
+// Bounded wait until counts[j] has reached seq << kCountShift (wrapping compare) for every
+// j < n, each read with system-scope acquire; false after timeout_ns.
+__device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsigned int seq, uint64_t timeout_ns)
+{
+    const unsigned long long target = (unsigned long long)seq << kCountShift;
+    const uint64_t t0 = tc::globaltimer_ns();
+    for (int j = 0; j < n; j++) {
+        for (;;) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counts + j) : "memory");
+            if ((long long)(v - target) >= 0) break;
+            if (tc::globaltimer_ns() - t0 > timeout_ns) return false;
+            __nanosleep(32);
+        }
+    }
+    return true;
 }
 
 // ----------------------------------------------------------------------------- prep
@@ -335,6 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ digitizers
         const int dtid = threadIdx.x - kFirstDig * 32;  // 0..127
         pdl_wait();  // x (and the prep kernel's exponents) are ready
+        if (p.po.wait_seq) {
+            // x is the gathered output of the previous call: wait until every rank's part landed
+            if (dtid == 0 && !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq, kPeerTimeoutNs)) {
+                atomicOr(&g_kernel_error_i8, 2);
+                raise_error(abort);
+            }
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
         if (p.fused_exps) {
             // Few tokens: every CTA finds the per-token exponents itself (the prep kernel's
             // rule: fp16 e = 24; fp32 e = 39 - floor(log2 max|x|); INT_MIN if any Inf/NaN).
@@ -389,8 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 asm volatile("bar.sync 2, 128;" ::: "memory");
             }
-            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents ready for the epilogue
         }
+        if (p.fused_exps || p.po.wait_seq)
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents / peers' outputs ready for the epilogue
         const int* exps = p.fused_exps ? s_exps : p.exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
@@ -445,9 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         pdl_wait();  // exps come from the prep kernel
         // the per-token exponents, once per CTA (they are read for every output)
-        if (p.fused_exps) {
-            asm volatile("bar.sync 3, 256;" ::: "memory");  // computed by the digitizers
-        } else {
+        if (p.fused_exps || p.po.wait_seq)
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents / peers' outputs ready
+        if (!p.fused_exps) {
             if (threadIdx.x - kFirstEpi * 32 < p.M) s_exps[threadIdx.x - kFirstEpi * 32] = p.exps[threadIdx.x - kFirstEpi * 32];
             asm volatile("bar.sync 1, 128;" ::: "memory");
         }
@@ -608,24 +637,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, C::kTmemCols);
     }
-    if (p.po.done_ctr && threadIdx.x == 0) {
-        // The last CTA to finish publishes this rank's slice to every rank: flags[r][rank] = seq.
-        // The barrier above orders every thread's output stores (local and peer) before this
-        // thread's system-scope fence, which makes them visible before the counter moves.
-        __threadfence_system();
-        const unsigned int prev = atomicAdd(p.po.done_ctr, 1u);
-        if (prev == gridDim.x - 1) {
-            *p.po.done_ctr = 0;  // ready for the next launch
-            __threadfence_system();
-            if (atomicAdd(&g_kernel_error_i8, 0) == 0) {  // a timed-out launch publishes nothing
-                // this rank's own flag last: once it is seen, the launch has no stores left
-                for (int i = 1; i <= p.po.ndst; i++) {
-                    const int d = (p.po.rank + i) % p.po.ndst;
-                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.po.flags[d] + p.po.rank),
-                                 "r"(p.po.seq)
-                                 : "memory");
-                }
-            }
+    if (p.po.publish && threadIdx.x == 0 && !*abort) {
+        // This CTA's output stores (every thread's, ordered before this point by the barrier
+        // above) are released to every rank together with its share of the call's count; the
+        // shares of the grid sum to 2^kCountShift.  This rank's own count last.  A CTA that
+        // gave up on a bounded wait publishes nothing, so its call never completes anywhere.
+        const unsigned long long share =
+            blockIdx.x == 0 ? (1ull << kCountShift) - (unsigned long long)(gridDim.x - 1) : 1ull;
+        for (int i = 1; i <= p.po.ndst; i++) {
+            const int d = (p.po.rank + i) % p.po.ndst;
+            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p.po.counts[d] + p.po.rank), "l"(share)
+                         : "memory");
         }
     }
 }
@@ -644,6 +666,35 @@ bool make_i8_map(CUtensorMap* m, const void* base, size_t K, size_t rows, int bo
     d.dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8;
     d.swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
     return tmap_2d(m, d);
+}
+
+// Grid size.  All SMs share HBM, so the stream needs enough of them (one SM pulls ~75 GB/s with
+// its 3-stage ring), but every extra CTA on a tile is one more stream-K piece whose partial the
+// last piece must fetch (four pieces per round trip of ~1 us).  Few-tile long-K shapes (a 7B
+// down projection sharded 8 ways: 4 tiles of 37 K-stages) would otherwise split each tile into
+// dozens of pieces; this takes the grid (all SMs, or a whole number of CTAs per tile) with the
+// lowest estimated stream + fixup time, preferring more CTAs on ties.
+long long pick_grid_i8(long long tiles, long long kbpt, long long weight_bytes, int num_sms)
+{
+    const long long units = tiles * kbpt;
+    const long long all = units < num_sms ? units : num_sms;
+    auto est = [&](long long G) {
+        const double bw = std::min(6.5e12, (double)G * 7.5e10);  // B/s (measured: ~75 GB/s per SM)
+        const long long pieces = (G + tiles - 1) / tiles;
+        const double fix = pieces > 1 ? 1.0e-6 * (1.0 + (double)((pieces - 1 + 3) / 4)) : 0.0;
+        return (double)weight_bytes / bw + fix;
+    };
+    long long best = all;
+    double best_t = est(all);
+    for (long long p = 1; tiles * p < all; p++) {
+        const long long G = tiles * p;
+        const double t = est(G);
+        if (t < best_t * 0.97) {  // clearly better only: prefer the larger grid on near ties
+            best = G;
+            best_t = t;
+        }
+    }
+    return best;
 }
 
 int pick_nc(size_t M)
@@ -695,7 +746,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.res = a.res;
     p.out = a.out;
     p.exps = sc.exps;
-    p.fused_exps = (a.M <= kFusedExpTokens && a.K <= kFusedExpMaxK) ? 1 : 0;
+    p.fused_exps = gemv_i8_fused_exps(a) ? 1 : 0;
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -713,7 +764,8 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         p.po.ldo = (long long)a.N;
         p.po.ocol0 = 0;
     }
-    const int G = (int)((p.units < num_sms) ? p.units : num_sms);
+    if (!p.fused_exps) p.po.wait_seq = 0;  // the prep kernel reads x first: the caller waits before it
+    const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
         sc.exps_count < a.M)
         return cudaErrorMemoryAllocation;
@@ -741,6 +793,8 @@ cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& sc, 
 
 int gemv_i8_max_tokens() { return kMaxTokens; }
 
+bool gemv_i8_fused_exps(const LinearArgs& a) { return a.M <= (size_t)kFusedExpTokens && a.K <= kFusedExpMaxK; }
+
 bool gemv_i8_supports(const LinearArgs& a)
 {
     const size_t xa = a.in_dtype == kF16 ? 8 : 16;  // 4-element vector loads of x
@@ -755,8 +809,7 @@ void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, s
     const int NC = pick_nc(a.M);
     const int BK = pick_bk_i8(NC);
     const long long tiles = (long long)((a.N + kTileRows - 1) / kTileRows);
-    const long long units = tiles * (long long)((a.K + BK - 1) / BK);
-    const long long G = units < num_sms ? units : num_sms;
+    const long long G = pick_grid_i8(tiles, (long long)((a.K + BK - 1) / BK), (long long)a.N * (long long)a.K, num_sms);
     *ws_floats = (size_t)(2 * G * NC * kTileRows);
     *counters = (size_t)tiles;
     *dig_bytes = 0;
