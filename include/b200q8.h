@@ -121,7 +121,8 @@ B200Q8_API int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* in
                                         b200q8_stream_t stream);
 
 /* Device error word of the current device: bit 0 is set when a bounded wait
- * inside the tensor-core kernel gave up (its outputs are then invalid).
+ * inside a tensor-core kernel gave up; bit 1 when a sharded call's wait for
+ * the peers' outputs ran out (2 s).  Either way the outputs are invalid.
  * clear != 0 resets it.  Synchronises with the device. */
 B200Q8_API int b200q8_kernel_error(int* code, int clear);
 
@@ -203,15 +204,16 @@ B200Q8_API int b200q8_comm_sym_free(b200q8_comm* comm, void* local);
 
 /* Sharded layer with the gather fused into the GEMV: each rank's kernel stores
  * its [M, rows] slice straight into columns [row0, row0 + rows) of `out` on
- * EVERY rank (peer stores over NVLink), then releases a flag on each rank;
- * a one-thread wait kernel on `stream` acquires the peers' flags (bounded:
+ * EVERY rank (peer stores over NVLink); every CTA then adds its share of the
+ * call's completion count on each rank (system-scope release reduction), and
+ * a one-thread wait kernel on `stream` acquires every rank's count (bounded:
  * 2 s, then bit 1 of b200q8_kernel_error).  `out` [M, N] of out_dtype must
  * lie inside one b200q8_comm_sym_alloc buffer at the same offset on every
  * rank.  M <= 42; K % 16 == 0 and 16 <= K <= 131072; every rank must own rows.
  * A peer may run one call ahead of this rank, so consecutive calls must use
  * different `out` buffers (double-buffer) unless the caller has finished
  * reading the previous result before the peers can start the next call.
- * The first call allocates the flags (collective: all ranks make it). */
+ * The first call allocates the completion counts (collective: all ranks make it). */
 B200Q8_API int b200q8_linear_q8_sharded_p2p(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
                                             int in_dtype, const int8_t* w_shard, const float* scales_shard,
                                             const float* bias_shard, size_t M, size_t N, size_t K,
@@ -219,10 +221,9 @@ B200Q8_API int b200q8_linear_q8_sharded_p2p(b200q8_comm* comm, void* out, int ou
 
 /* As b200q8_linear_q8_sharded_p2p, with B200Q8_P2P_DEFER_WAIT in `flags`: the call enqueues no
  * wait, so `out` is NOT yet complete in stream order.  The wait is owed by the communicator and
- * paid by its next gathered call (inside that call's GEMV when it has few short tokens, M <= 4
- * and K <= 4096, else as a wait kernel ahead of it) or by b200q8_comm_wait.  Any other consumer
- * of `out` must come after b200q8_comm_wait on the same stream.  Chains of deferred calls must
- * stay on one stream. */
+ * paid by its next gathered call (inside the first of that call's kernels that reads its input)
+ * or by b200q8_comm_wait.  Any other consumer of `out` must come after b200q8_comm_wait on the
+ * same stream.  Chains of deferred calls must stay on one stream. */
 #define B200Q8_P2P_DEFER_WAIT 1u
 B200Q8_API int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
                                                int in_dtype, const int8_t* w_shard, const float* scales_shard,

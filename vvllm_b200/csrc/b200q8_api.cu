@@ -971,17 +971,13 @@ int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, co
     gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
     TcScratch scratch;
     if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
-    // A deferred wait of the previous call is owed before this call reads its input: inside the
-    // GEMV when it reads x only in-kernel, else as the wait kernel ahead of it.
+    // A deferred wait of the previous call is owed before this call reads its input: it is paid
+    // inside whichever of this call's kernels reads x first (the GEMV, or its prep kernel).
     if (c->pending) {
-        if (gemv_i8_fused_exps(a)) {
-            po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
-            po.wait_n = G;
-            po.wait_seq = c->pending;
-            c->pending = 0;
-        } else if ((st = b200q8_comm_wait(c, stream))) {
-            return st;
-        }
+        po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
+        po.wait_n = G;
+        po.wait_seq = c->pending;
+        c->pending = 0;
     }
     if ((e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream)) != cudaSuccess)
         return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");

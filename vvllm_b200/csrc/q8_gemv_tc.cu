@@ -135,14 +135,21 @@ __device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsign
 // One CTA per token: the exponent e (fp16: 24; fp32: 39 - floor(log2(max|x|))) or
 // INT_MIN when the row holds Inf/NaN.
 template <typename XT>
-__global__ void __launch_bounds__(1024) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps)
+__global__ void __launch_bounds__(1024) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps,
+                                                    const unsigned long long* wait_counts, int wait_n,
+                                                    unsigned int wait_seq)
 {
     pdl_launch_dependents();  // the GEMV may start streaming weights right away
     pdl_wait();               // x is written by the previous kernel
     __shared__ float red[32];
     __shared__ int bad_any;
     const int m = blockIdx.x;
-    if (threadIdx.x == 0) bad_any = 0;
+    if (threadIdx.x == 0) {
+        bad_any = 0;
+        // x is the gathered output of a deferred call: every rank's part must have landed
+        if (wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, kPeerTimeoutNs))
+            atomicOr(&g_kernel_error_i8, 2);
+    }
     __syncthreads();
     float mx = 0.0f;
     int bad = 0;
@@ -764,7 +771,9 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         p.po.ldo = (long long)a.N;
         p.po.ocol0 = 0;
     }
-    if (!p.fused_exps) p.po.wait_seq = 0;  // the prep kernel reads x first: the caller waits before it
+    // Without in-kernel exponents the prep kernel reads x first: it pays the deferred wait.
+    const unsigned int prep_wait_seq = p.fused_exps ? 0u : p.po.wait_seq;
+    if (!p.fused_exps) p.po.wait_seq = 0;
     const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
         sc.exps_count < a.M)
@@ -772,7 +781,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M), dim3(1024), 0, stream, a.pdl,
-                  reinterpret_cast<const XT*>(a.x), (int)a.K, sc.exps);
+                  reinterpret_cast<const XT*>(a.x), (int)a.K, sc.exps, p.po.wait_counts, p.po.wait_n, prep_wait_seq);
     if (e != cudaSuccess) return e;
     return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
 }
