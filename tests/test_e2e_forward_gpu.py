@@ -1,0 +1,52 @@
+"""The reference's own Qwen2 forward pass with the B200 hot path behind its Backend interface.
+
+oracle/_ref/libvvllm_e2e.so is built from the reference sources where they lie (model.cc,
+transformer.cc, tensor.cc, kv_cache_cpu.cc, backend_naive.cc, quantize.cc) plus the adapter
+vvllm_b200/adapter/backend_b200.cc, which overrides only Backend::linear_q8 / linear_q8_add
+(include/vvllm/backend/backend.h:62-78) and sends them to libb200q8.  The same seeded
+Qwen2.5-0.5B-shaped model (2 layers, quantized projections, tied fp32 lm_head) runs a 5-token
+prompt and 3 decode steps with the reference CPU backend and with the adapter; the logits must
+agree (fp32 activations: every linear is within 1e-5 normwise of the reference, and the
+differences pass through RMSNorm, attention and the MLP of two layers) and pick the same token.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+E2E = os.path.join(HERE, "..", "oracle", "_ref", "libvvllm_e2e.so")
+VOCAB = 151936
+TOL = 1e-4  # normwise per logits row, after two transformer layers
+
+
+def _run(lib, use_b200, tokens, n_prompt, n_decode, layers=2):
+    out = np.zeros((1 + n_decode, VOCAB), dtype=np.float32)
+    calls = ctypes.c_longlong(0)
+    st = lib.vvllm_e2e_logits(int(use_b200), layers, tokens.ctypes.data, n_prompt, n_decode, out.ctypes.data,
+                              ctypes.byref(calls))
+    assert st == 0
+    return out, calls.value
+
+
+def test_qwen2_forward_with_b200_backend(cuda):
+    if not os.path.exists(E2E):
+        pytest.skip("oracle/_ref/libvvllm_e2e.so not built (needs the reference sources at build time)")
+    import vvllm_b200 as v
+
+    v.lib()  # the adapter links the in-tree libb200q8.so
+    lib = ctypes.CDLL(E2E)
+    lib.vvllm_e2e_logits.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_void_p, ctypes.c_void_p]
+    lib.vvllm_e2e_logits.restype = ctypes.c_int
+    tokens = np.array([151643, 9707, 11, 1879, 0, 17, 42, 3000], dtype=np.int32)
+    ref, _ = _run(lib, False, tokens, 5, 3)
+    got, calls = _run(lib, True, tokens, 5, 3)
+    assert calls == 2 * 6 * 4  # q, k, v, o(+res), gate_up, down(+res) per layer per forward call
+    for i in range(ref.shape[0]):
+        err = np.max(np.abs(got[i] - ref[i])) / np.max(np.abs(ref[i]))
+        assert err <= TOL, (i, err)
+        assert int(np.argmax(got[i])) == int(np.argmax(ref[i])), i
