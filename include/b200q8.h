@@ -120,6 +120,17 @@ B200Q8_API int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* in
                                         const void* residual, size_t M, size_t N, size_t K,
                                         b200q8_stream_t stream);
 
+/* Quantized lm_head with greedy decoding fused in: argmax[m] = the index of the largest of
+ * out[m, 0..N) where out = b200q8_linear_q8(...), computed in the same kernel.  The order is the
+ * reference CPU sampler's (SamplerCPU::sample, temperature 0: std::max_element over the logits,
+ * src/sampler/sampler.cc:20-24): the first maximum wins, NaNs are skipped unless the first
+ * logit is NaN (then 0); values are compared as stored in out_dtype.  out may be NULL (the logits
+ * are then not written).  argmax is an int[M] device array.  M <= 42, K % 16 == 0,
+ * 16 <= K <= 131072.  Stream-ordered; calls on one stream share a small scratch. */
+B200Q8_API int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dtype,
+                                       const int8_t* weight, const float* scales, const float* bias,
+                                       size_t M, size_t N, size_t K, int* argmax, b200q8_stream_t stream);
+
 /* Device error word of the current device: bit 0 is set when a bounded wait
  * inside a tensor-core kernel gave up; bit 1 when a sharded call's wait for
  * the peers' outputs ran out (2 s).  Either way the outputs are invalid.

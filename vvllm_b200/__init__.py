@@ -16,6 +16,7 @@ from ._lib import (  # noqa: F401
     launch_count,
     linear_q8,
     linear_q8_add,
+    linear_q8_argmax,
     linear_q8_ex,
     kernel_error,
     ALGO_AUTO,

@@ -59,6 +59,7 @@ _SIGS = {
     "b200q8_linear_q8_sharded_p2p_ex": (
         [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, ctypes.c_uint, _vp], _int),
     "b200q8_comm_wait": ([_vp, _vp], _int),
+    "b200q8_linear_q8_argmax": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp], _int),
 }
 
 # Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
@@ -139,6 +140,16 @@ def linear_q8_add(out, x, w, scales, bias, residual, stream=None) -> None:
     _check(lib().b200q8_linear_q8_add(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x),
                                       _addr(w), _addr(scales), _addr(bias), _addr(residual), M, N,
                                       K, _stream(stream)))
+
+
+def linear_q8_argmax(out, x, w, scales, bias, argmax, out_dtype=None, stream=None) -> None:
+    """argmax[m] (int32 device tensor) = greedy argmax of out[m, :] = linear_q8(x, w); out may be
+    None (logits not written; then out_dtype picks the comparison precision, default fp32)."""
+    M, K = x.shape
+    N = w.shape[0]
+    odt = _dtype_code(out) if out is not None else (F32 if out_dtype is None else out_dtype)
+    _check(lib().b200q8_linear_q8_argmax(_addr(out), odt, _addr(x), _dtype_code(x), _addr(w), _addr(scales),
+                                         _addr(bias), M, N, K, _addr(argmax), _stream(stream)))
 
 
 ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_TC_I8 = 0, 1, 2, 3

@@ -109,6 +109,7 @@ std::unordered_map<ScratchKey, TcScratch, ScratchKeyHash> g_scratch;
 
 struct ScratchNeed {
     size_t ws = 0, counters = 0, dig = 0, exps = 0;
+    bool amax = false;
 };
 
 // Grows one device buffer of `s` to at least `need` elements (never shrinks).
@@ -150,6 +151,11 @@ int get_scratch(const ScratchNeed& need, int num_sms, cudaStream_t stream, TcScr
         (st = grow(&s.dig, &s.dig_bytes, need.dig, (size_t)4 * 64 * 32768, stream, false, "digits")) ||
         (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)64, stream, false, "exponents")))
         return st;
+    if (need.amax && !s.amax) {  // argmax keys + done counter, zero at rest
+        size_t have = 0;
+        if ((st = grow(&s.amax, &have, (size_t)kMaxArgmaxTokens + 1, 0, stream, true, "argmax")))
+            return st;
+    }
     *out = s;
     return B200Q8_OK;
 }
@@ -161,6 +167,8 @@ int reset_scratch_counters(int dev)
     for (auto& kv : g_scratch) {
         if (kv.first.dev != dev || !kv.second.counter_ptr) continue;
         cudaError_t e = cudaMemset(kv.second.counter_ptr, 0, kv.second.counters * sizeof(int));
+        if (e == cudaSuccess && kv.second.amax)
+            e = cudaMemset(kv.second.amax, 0, (kMaxArgmaxTokens + 1) * sizeof(unsigned long long));
         if (e != cudaSuccess) return cuda_fail(e, "reset scratch counters");
     }
     return B200Q8_OK;
@@ -396,6 +404,57 @@ int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* inp, int in_d
                             "8-byte (fp16) / 16-byte (fp32) aligned input (K=%zu)", K);
         default: return cuda_fail(e, "linear_q8_noalloc");
     }
+}
+
+int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
+                            const float* scales, const float* bias, size_t M, size_t N, size_t K, int* argmax,
+                            b200q8_stream_t stream)
+{
+    if (!valid_dtype(out_dtype) || !valid_dtype(in_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8_argmax: dtype must be B200Q8_F32 or B200Q8_F16");
+    if (M == 0) return B200Q8_OK;
+    if (N == 0) return fail(B200Q8_ERR_INVALID, "linear_q8_argmax: N = 0 has no argmax");
+    if (!inp || !weight || !scales || !argmax)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_argmax: null inp/weight/scales/argmax");
+    if (K == 0 || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX || N * K / K != N)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_argmax: bad sizes (N=%zu K=%zu)", N, K);
+    if (M > (size_t)gemv_i8_max_tokens() || M > (size_t)kMaxArgmaxTokens)
+        return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_argmax: at most %d tokens (M=%zu)", gemv_i8_max_tokens(), M);
+    if (out) {
+        const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4, ib = in_dtype == B200Q8_F16 ? 2 : 4;
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t i0 = (uintptr_t)inp, i1 = i0 + M * K * ib;
+        if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8_argmax: inp overlaps out");
+    }
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+    LinearArgs a;
+    a.x = inp;
+    a.w = weight;
+    a.scales = scales;
+    a.bias = bias;
+    a.out = out;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.in_dtype = in_dtype;
+    a.out_dtype = out_dtype;
+    a.pdl = true;
+    if (!gemv_i8_supports(a))
+        return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_argmax: needs K %% 16 == 0, 16 <= K <= 131072, a 16-byte "
+                                            "aligned weight and an 8-byte (fp16) / 16-byte (fp32) aligned input");
+    ScratchNeed need;
+    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+    need.amax = true;
+    TcScratch scratch;
+    if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
+    a.amax_keys = scratch.amax;
+    a.amax_done = reinterpret_cast<unsigned int*>(scratch.amax + kMaxArgmaxTokens);
+    a.amax_out = argmax;
+    const cudaError_t e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "linear_q8_argmax: launch");
+    return B200Q8_OK;
 }
 
 int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype,

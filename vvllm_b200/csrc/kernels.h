@@ -46,6 +46,11 @@ struct LinearArgs {
     int in_dtype = kF32, out_dtype = kF32;
     bool pdl = false;               // launch with programmatic stream serialization
     const P2POut* p2p = nullptr;    // int8 digit GEMV only: gather into peers' outputs
+    // int8 digit GEMV only: greedy argmax of each token's outputs into amax_out[M] (keys and
+    // counter are scratch that starts at zero and is left at zero).  out may then be null.
+    unsigned long long* amax_keys = nullptr;
+    unsigned int* amax_done = nullptr;
+    int* amax_out = nullptr;
 };
 
 // One thread waits (bounded, `timeout_ns`) until counts[j] has reached seq << kCountShift for
@@ -76,7 +81,9 @@ struct TcScratch {
     size_t dig_bytes = 0;
     int* exps = nullptr;         // per-token exponents [M]
     size_t exps_count = 0;
+    unsigned long long* amax = nullptr;  // argmax keys [kMaxArgmaxTokens] + a counter word, zero at rest
 };
+constexpr int kMaxArgmaxTokens = 64;
 
 // Tensor-core GEMV for M <= gemv_i8_max_tokens() with exact 4-digit int8
 // activations (fp16 or fp32 inputs) and kind::i8 MMAs on the raw int8 weights.

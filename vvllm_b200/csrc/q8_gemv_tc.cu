@@ -86,6 +86,11 @@ struct DigParams {
     long long units;
     P2POut po;        // output placement: local only (ndst = 1) or every rank's copy
     int fused_exps;   // exponents computed in-kernel (few tokens) instead of by the prep kernel
+    // Greedy argmax over each token's outputs (null: none): packed (value, index) keys, zero
+    // between launches; the launch's last CTA turns them into indices and re-zeroes them.
+    unsigned long long* amax_keys;  // [M]
+    unsigned int* amax_done;        // CTAs finished, zero between launches
+    int* amax_out;                  // [M] result
 };
 
 template <int NC, int BK, int S>
@@ -99,7 +104,8 @@ struct DigCfg {
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                      : kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kNumBars = 3 * S + 4 + 1;  // full, dfull, empty per stage; acc x4; drain
-    static constexpr int kSmemBytes = 1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 32;
+    static constexpr int kSmemBytes =
+        1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 32 + 8 * kMaxTokens + 8;
     static_assert(NC % 16 == 0 && NC >= 16 && NC <= 256, "kind::i8 N for M=128");
     static_assert(BK % 128 == 0, "whole 128-byte boxes");
     static_assert(kColsNeeded <= 512, "TMEM overflow");
@@ -208,15 +214,34 @@ __device__ __forceinline__ float recombine(const long long (&dsum)[kDigits], int
 
 // v = acc * scale (+ bias) (+ res[m, n]) stored at column ocol0 + n of row m in every
 // output copy (one local copy, or each rank's copy over NVLink for the sharded gather).
+// Returns the output as stored (rounded to OT).
 template <typename OT>
-__device__ __forceinline__ void epi_out(const DigParams& p, int m, int n, float acc, float scale, float bias,
-                                        bool has_bias)
+__device__ __forceinline__ float epi_out(const DigParams& p, int m, int n, float acc, float scale, float bias,
+                                         bool has_bias)
 {
     float v = __fmul_rn(acc, scale);
     if (has_bias) v = __fadd_rn(v, bias);
     if (p.res) v = __fadd_rn(v, load_as_f32<OT>(reinterpret_cast<const OT*>(p.res) + (size_t)m * p.N + n));
     const size_t o = (size_t)m * p.po.ldo + p.po.ocol0 + n;
     for (int d = 0; d < p.po.ndst; d++) sk::store_out<OT>(reinterpret_cast<OT*>(p.po.dst[d]) + o, v);
+    if (sizeof(OT) == 2) v = __half2float(__float2half_rn(v));
+    return v;
+}
+
+// Greedy-argmax key of output n with stored value v: larger key = larger value, then smaller
+// index.  The order is std::max_element's over the row (src/sampler/sampler.cc:20-24): the first
+// maximum wins, NaNs are never greater than anything -- except a NaN at index 0, which
+// std::max_element keeps, so it gets the largest key.  -0 compares equal to +0.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n)
+{
+    uint32_t ord;
+    if (v != v) {
+        ord = n == 0 ? 0xFFFFFFFFu : 0u;
+    } else {
+        const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+        ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    }
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
 }
 
 // ----------------------------------------------------------------------------- GEMV
@@ -236,6 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]
     int* s_exps = reinterpret_cast<int*>(tmem_holder + 4);                          // [kMaxTokens]
     float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [8] exponent reduction
+    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(                 // [kMaxTokens] argmax keys
+        (reinterpret_cast<uintptr_t>(s_red + 8) + 7) & ~static_cast<uintptr_t>(7));
 
     const uint32_t bar0 = tc::smem_u32(bars);
     const uint32_t full0 = bar0, dfull0 = bar0 + 8u * S, empty0 = bar0 + 16u * S, accfull0 = bar0 + 24u * S,
@@ -481,6 +508,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         pdl_wait();  // exps come from the prep kernel
         // the per-token exponents, once per CTA (they are read for every output)
+        if (p.amax_keys) {
+            if (threadIdx.x - kFirstEpi * 32 < p.M) s_best[threadIdx.x - kFirstEpi * 32] = 0ull;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
         if (p.fused_exps || p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents / peers' outputs ready
         if (!p.fused_exps) {
@@ -605,7 +636,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                                 for (int i = 0; i < kDigits; i++) ds[i] += vv[u][i];
                         }
-                        if (nv) epi_out<OT>(p, m, n, recombine(ds, s_exps[m]), scale, bias, has_bias);
+                        const float vout = nv ? epi_out<OT>(p, m, n, recombine(ds, s_exps[m]), scale, bias, has_bias)
+                                              : 0.0f;
+                        if (p.amax_keys) {  // this warp's best output of token m, then the CTA's
+                            unsigned long long key = nv ? argmax_key(vout, n) : 0ull;
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                                key = other > key ? other : key;
+                            }
+                            if (lane == 0) atomicMax(s_best + m, key);
+                        }
                     }
                 }
                 if (last) {
@@ -633,6 +673,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             seg++;
         }
         if (!ok) raise_error(abort);
+        if (p.amax_keys) {  // this CTA's best per token into the launch's keys
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (etid < p.M && s_best[etid]) atomicMax(p.amax_keys + etid, s_best[etid]);
+        }
         pdl_launch_dependents();
     }
 
@@ -643,6 +687,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, C::kTmemCols);
+    }
+    if (p.amax_keys && threadIdx.x == 0) {
+        // the launch's last CTA turns the keys into indices and leaves them zero again
+        __threadfence();
+        const unsigned int prev = atomicAdd(p.amax_done, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            for (int m = 0; m < p.M; m++) {
+                const unsigned long long k = atomicExch(p.amax_keys + m, 0ull);
+                p.amax_out[m] = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+            }
+            *p.amax_done = 0;
+        }
     }
     if (p.po.publish && threadIdx.x == 0 && !*abort) {
         // This CTA's output stores (every thread's, ordered before this point by the barrier
@@ -754,6 +811,9 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.out = a.out;
     p.exps = sc.exps;
     p.fused_exps = gemv_i8_fused_exps(a) ? 1 : 0;
+    p.amax_keys = a.amax_keys;
+    p.amax_done = a.amax_done;
+    p.amax_out = a.amax_out;
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -766,7 +826,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         p.po = *a.p2p;
     } else {  // one local [M, N] output
         p.po = P2POut();
-        p.po.ndst = 1;
+        p.po.ndst = a.out ? 1 : 0;  // no output copy: argmax only
         p.po.dst[0] = a.out;
         p.po.ldo = (long long)a.N;
         p.po.ocol0 = 0;
