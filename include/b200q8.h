@@ -88,11 +88,11 @@ B200Q8_API int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, i
                          b200q8_stream_t stream);
 
 /* Kernel choice for b200q8_linear_q8_ex. */
-#define B200Q8_ALGO_AUTO 0  /* M <= 16: TC_I8; larger M: TC for fp16, TC_I8 (64-token groups) for fp32 */
+#define B200Q8_ALGO_AUTO 0  /* M <= 16: TC_I8; larger M: TC for fp16, TC_I8 (42-token groups) for fp32 */
 #define B200Q8_ALGO_SIMT 1  /* streaming SIMT GEMV (any dtype, any K; groups of <= 4 tokens) */
 #define B200Q8_ALGO_TC 2    /* tcgen05 kind::f16 GEMM, weights dequantized into TMEM (fp16 activations) */
-#define B200Q8_ALGO_TC_I8 3 /* tcgen05 kind::i8 GEMV on raw int8 weights, activations as exact 4-digit int8
-                               (fp16 or fp32 activations, groups of <= 64 tokens, K <= 131072) */
+#define B200Q8_ALGO_TC_I8 3 /* tcgen05 kind::i8 GEMV on raw int8 weights, activations as exact 6-digit int8
+                               (fp16 or fp32 activations, groups of <= 42 tokens, K <= 131072) */
 
 /* Both of the above in one call (residual may be NULL) with an explicit
  * kernel choice; B200Q8_ERR_UNSUPPORTED if the chosen kernel cannot take the
@@ -130,6 +130,42 @@ B200Q8_API int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* in
 B200Q8_API int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dtype,
                                        const int8_t* weight, const float* scales, const float* bias,
                                        size_t M, size_t N, size_t K, int* argmax, b200q8_stream_t stream);
+
+/* Projections with the elementwise op before them fused in.  vvllm runs, per layer,
+ *   norm = rms_norm(x) then q/k/v (or gate_up) = linear_q8(norm)
+ *     (include/vvllm/model/transformer.h:135-144, :167-169; rms_norm per token,
+ *      src/model/transformer.cc:40-50, src/backend/backend_naive.cc:67-75), and
+ *   h = silu_mul(gate_up[:, :K], gate_up[:, K:]) then x = linear_q8_add(h, x)
+ *     (transformer.h:171-188; backend_naive.cc:293-300).
+ * These compute the same results with the elementwise op done where the projection reads its
+ * activations: for the int8 decode GEMV (up to 16 fp16 / any number of fp32 tokens) it runs
+ * inside that kernel, so the normalised / gated activations never go to memory and the extra
+ * launch disappears; for the fp16 prefill GEMM it runs first as its own kernel into scratch.
+ * Arithmetic: rms = sqrt(sum_k x^2 / K + eps) (sum taken in double, one fixed order), then
+ * x / rms * w; silu_mul = (g / (1 + exp(-g))) * u.  With fp16 activations the norm weight is
+ * rounded to fp16 and the result to fp16, as vvllm's fp16 backend does
+ * (src/backend/backend_cuda.cc:135-145, cuda_kernels.cu:876-910).  Results are bit-identical to
+ * b200q8_rms_norm / b200q8_silu_mul followed by b200q8_linear_q8 / b200q8_linear_q8_add.
+ *   rms_norm_linear_q8:    x [M, K] (in_dtype), norm_weight [K] fp32, out [M, N].
+ *   silu_mul_linear_q8_add: gate_up [M, 2K] (in_dtype; gate = columns 0..K-1, up = K..2K-1),
+ *                           residual [M, N] (out_dtype) or NULL, may equal out.
+ * K % 4 == 0; x / gate_up 8-byte (fp16) or 16-byte (fp32) aligned; norm_weight 16-byte aligned. */
+B200Q8_API int b200q8_rms_norm_linear_q8(void* out, int out_dtype, const void* x, int in_dtype,
+                                         const float* norm_weight, float eps, const int8_t* weight,
+                                         const float* scales, const float* bias, size_t M, size_t N, size_t K,
+                                         b200q8_stream_t stream);
+B200Q8_API int b200q8_silu_mul_linear_q8_add(void* out, int out_dtype, const void* gate_up, int in_dtype,
+                                             const int8_t* weight, const float* scales, const float* bias,
+                                             const void* residual, size_t M, size_t N, size_t K,
+                                             b200q8_stream_t stream);
+
+/* The elementwise ops alone, same arithmetic (vvllm Backend::rms_norm applied per token, as
+ * rms_norm_seq does, src/model/transformer.cc:40-50; Backend::silu_mul over each gate_up row,
+ * transformer.h:175-180): out [M, K] in dtype from x [M, K] / gate_up [M, 2K] in dtype. */
+B200Q8_API int b200q8_rms_norm(void* out, const void* x, int dtype, const float* norm_weight, float eps, size_t M,
+                               size_t K, b200q8_stream_t stream);
+B200Q8_API int b200q8_silu_mul(void* out, const void* gate_up, int dtype, size_t M, size_t K,
+                               b200q8_stream_t stream);
 
 /* Device error word of the current device: bit 0 is set when a bounded wait
  * inside a tensor-core kernel gave up; bit 1 when a sharded call's wait for

@@ -59,6 +59,27 @@ class _Lib:
         self._lmt.argtypes = [_vp, _vp, _vp, _vp, _vp, _c_size, _c_size, _c_size, ctypes.c_int]
         for f in (self._q, self._l, self._la, self._lmt):
             f.restype = ctypes.c_int
+        self._rn = getattr(self.lib, f"{p}rms_norm")
+        self._sm = getattr(self.lib, f"{p}silu_mul")
+        self._rn.argtypes = [_vp, _vp, _vp, _c_size, _c_size, ctypes.c_float]
+        self._sm.argtypes = [_vp, _vp, _c_size, _c_size]
+
+    # backend_naive.cc:67-75 per token (transformer.cc:40-50): [M, K] -> [M, K]
+    def rms_norm(self, x, w, eps):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        M, K = x.shape
+        y = np.empty((M, K), dtype=np.float32)
+        self._rn(_ptr(y), _ptr(x), _ptr(w), M, K, float(eps))
+        return y
+
+    # backend_naive.cc:293-300 per [gate | up] row (transformer.h:175-180): [M, 2K] -> [M, K]
+    def silu_mul(self, gate_up):
+        gu = np.ascontiguousarray(gate_up, dtype=np.float32)
+        M, K2 = gu.shape
+        y = np.empty((M, K2 // 2), dtype=np.float32)
+        self._sm(_ptr(y), _ptr(gu), M, K2 // 2)
+        return y
 
     # quantize.cc:9-48 -- returns (int8 [N,K], fp32 scales [N])
     def quantize_per_channel(self, w: np.ndarray):

@@ -13,6 +13,10 @@
  *   q8o_linear_q8             src/backend/backend_naive.cc:155-291 (x86 AVX2+FMA
  *                             branch :216-274, epilogue :283-288)
  *   q8o_linear_q8_add         src/backend/backend_naive.cc:322-335 (+ add :43-49)
+ *   q8o_rms_norm              src/backend/backend_naive.cc:67-75, applied per token as
+ *                             rms_norm_seq does (src/model/transformer.cc:40-50)
+ *   q8o_silu_mul              src/backend/backend_naive.cc:293-300, applied to each
+ *                             [gate | up] row (include/vvllm/model/transformer.h:175-180)
  *
  * The AVX2 branch keeps 4 accumulators of 8 lanes over 32-wide K blocks,
  * combines them pairwise, folds 8 lanes to 4, then does two horizontal adds,
@@ -196,4 +200,38 @@ int q8o_linear_q8_mt(float* out, const float* inp, const int8_t* weight, const f
     free(th);
     free(jobs);
     return 0;
+}
+
+/* src/backend/backend_naive.cc:67-75 for each of M tokens: the sum of squares is a left fold in
+ * float (std::accumulate with acc + x * x, no contraction), rms = sqrt(sum / n + eps) (the float
+ * sum divided by n converted to float; sqrt in double and narrowed, which equals the correctly
+ * rounded float sqrt), then out = x / rms * w. */
+void q8o_rms_norm(float* out, const float* x, const float* w, size_t M, size_t K, float eps)
+{
+    for (size_t m = 0; m < M; m++) {
+        const float* xr = x + m * K;
+        float* o = out + m * K;
+        float sum = 0.0f;
+        for (size_t k = 0; k < K; k++) {
+            const float sq = xr[k] * xr[k];
+            sum = sum + sq;
+        }
+        const float rms = (float)sqrt((double)(sum / (float)K + eps));
+        for (size_t k = 0; k < K; k++) o[k] = xr[k] / rms * w[k];
+    }
+}
+
+/* src/backend/backend_naive.cc:293-300 for each of M rows of gate_up = [gate (K) | up (K)]:
+ * out = (g / (1 + exp(-g))) * u with the float exp. */
+void q8o_silu_mul(float* out, const float* gate_up, size_t M, size_t K)
+{
+    for (size_t m = 0; m < M; m++) {
+        const float* g = gate_up + m * 2 * K;
+        const float* u = g + K;
+        float* o = out + m * K;
+        for (size_t k = 0; k < K; k++) {
+            const float v = g[k];
+            o[k] = (v / (1.0f + expf(-v))) * u[k];
+        }
+    }
 }

@@ -8,6 +8,9 @@
 //   vvllm::quantize_per_channel   (include/vvllm/quantize/quantize.h:18)
 //   vvllm::BackendCPU::linear_q8  (src/backend/backend_naive.h:30-31)
 //   vvllm::BackendCPU::linear_q8_add (src/backend/backend_naive.h:35-37)
+//   vvllm::BackendCPU::rms_norm, silu_mul (src/backend/backend_naive.cc:67-75, :293-300),
+//     applied per token the way src/model/transformer.cc:40-50 and
+//     include/vvllm/model/transformer.h:175-180 apply them
 // It is used to pin oracle/q8_oracle.c bit-for-bit, to make the golden
 // fixtures under tests/golden/, and as the timed CPU baseline of bench.py.
 #include <cstddef>
@@ -42,6 +45,20 @@ int vref_linear_q8_add(float* out, const float* inp, const int8_t* weight, const
 {
     vvllm::BackendCPU be;
     be.linear_q8_add(out, inp, weight, scales, bias, residual, M, N, K);
+    return 0;
+}
+
+int vref_rms_norm(float* out, const float* x, const float* w, size_t M, size_t K, float eps)
+{
+    vvllm::BackendCPU be;
+    for (size_t m = 0; m < M; m++) be.rms_norm(out + m * K, x + m * K, w, K, eps);
+    return 0;
+}
+
+int vref_silu_mul(float* out, const float* gate_up, size_t M, size_t K)
+{
+    vvllm::BackendCPU be;
+    for (size_t m = 0; m < M; m++) be.silu_mul(out + m * K, gate_up + m * 2 * K, gate_up + m * 2 * K + K, K);
     return 0;
 }
 

@@ -14,6 +14,9 @@ called through oracle/ref_shim.cc.  Outputs:
   355-425) with the reference's exact results (float bit patterns in hex);
 * quantize_edge.npz  -- edge rows (zeros, NaN, +-Inf, subnormals, ties);
 * linear_small.npz   -- seeded small linear_q8 / linear_q8_add cases;
+* prologue_small.npz -- BackendCPU::rms_norm / silu_mul (backend_naive.cc:67-75, :293-300)
+  applied per token, on the reference tests' two rms_norm cases
+  (backend_naive_test.cc:199-236), seeded rows and edge rows;
 * digests.json       -- SHA-256 of the reference's outputs at full benchmark
   sizes for inputs regenerated from numpy seeds (tests rebuild the inputs and
   compare digests, so megabytes of data need not be committed).
@@ -172,12 +175,46 @@ def digests(ref: Reference) -> dict:
     return out
 
 
+def prologue_small(ref: Reference) -> dict:
+    data = {}
+    rng = np.random.default_rng(77)
+    # rms_norm: (x [M, K], w [K], eps)
+    rn = [
+        (np.full((1, 4), 2.0, np.float32), np.ones(4, np.float32), 1e-6),             # RmsNormUniform
+        (np.array([[1, 2, 3]], np.float32), np.array([0.5, 1, 2], np.float32), 1e-6),  # RmsNormWithWeight
+        (make_x(3, 896, 501), (1 + 0.1 * rng.standard_normal(896)).astype(np.float32), 1e-6),
+        (make_x(2, 3584, 502) * np.float32(40), rng.standard_normal(3584).astype(np.float32), 1e-5),
+    ]
+    edge = make_x(3, 64, 503)
+    edge[0] = 0.0                 # zero row: rms = sqrt(eps)
+    edge[1, 5] = np.float32(1e20)  # x^2 overflows: rms = inf
+    edge[2, ::7] = -edge[2, ::7]
+    rn.append((edge, rng.standard_normal(64).astype(np.float32), 1e-6))
+    for i, (x, w, eps) in enumerate(rn):
+        p = f"rn{i}_"
+        data[p + "x"], data[p + "w"], data[p + "eps"] = x, w, np.float32(eps)
+        data[p + "y"] = ref.rms_norm(x, w, eps)
+    # silu_mul: gate_up [M, 2K]
+    sm = [make_x(2, 2 * 896, 511) * np.float32(3), make_x(1, 2 * 4864, 512) * np.float32(8)]
+    g = np.array([-100, -88, -20, -1, -0.0, 0, 1e-30, 0.5, 1, 20, 88, 100, -87.5, 87.5, -3, 3], np.float32)
+    sm.append(np.concatenate([g, rng.standard_normal(16).astype(np.float32)])[None, :])
+    for i, gu in enumerate(sm):
+        p = f"sm{i}_"
+        data[p + "gu"] = gu
+        data[p + "y"] = ref.silu_mul(gu)
+    return data
+
+
 def main():
     ref = Reference()
+    if sys.argv[1:] == ["prologue"]:  # only the prologue fixtures
+        np.savez_compressed(os.path.join(HERE, "prologue_small.npz"), **prologue_small(ref))
+        return
     with open(os.path.join(HERE, "known_answers.json"), "w") as f:
         json.dump(known_answers(ref), f, indent=1)
     np.savez_compressed(os.path.join(HERE, "quantize_edge.npz"), **quantize_edges(ref))
     np.savez_compressed(os.path.join(HERE, "linear_small.npz"), **linear_small(ref))
+    np.savez_compressed(os.path.join(HERE, "prologue_small.npz"), **prologue_small(ref))
     with open(os.path.join(HERE, "digests.json"), "w") as f:
         json.dump(digests(ref), f, indent=1)
 

@@ -188,6 +188,28 @@ def test_i8_nonfinite_rows_give_nan(cuda, oracle):
         assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32
 
 
+def test_i8_prep_kernel_scratch_across_token_counts(cuda, oracle):
+    """Rows longer than 4096 take the prep kernel, several CTAs per token combining through
+    zero-at-rest words in the per-stream scratch.  Calls with different token counts in a row
+    (fp32: exponents differ per token; an Inf row in between) must each be right: no call may
+    leave those words dirty for the next, whatever its M."""
+    import vvllm_b200 as v
+
+    N, K = 320, 8192
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 95))
+    for M, seed in ((7, 96), (1, 97), (3, 98), (5, 99), (1, 100), (7, 101)):
+        x = make_x(M, K, seed) * np.float32(10.0 ** (seed % 5 - 2))
+        if M == 5:
+            x[2, 11] = np.inf
+        y, xe, _ = run_gpu(cuda, x, q, s, None, None, algo=v.ALGO_TC_I8)
+        ref = oracle_ref(oracle, xe, q, s, None, None)
+        for i in range(M):
+            if M == 5 and i == 2:
+                assert np.all(np.isnan(y[i]))
+            else:
+                assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32, (M, i)
+
+
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs
 
 

@@ -150,3 +150,26 @@ def test_oracle_rows_match_full(oracle):
     rows = np.array([0, 5, 96, 50], np.int64)
     part = oracle.linear_q8_rows(x, q, s, b, rows)
     assert np.array_equal(_bits(part), _bits(full[:, rows]))
+
+
+def test_prologue_golden(oracle):
+    """rms_norm / silu_mul restatements equal the reference's outputs bit for bit (NaN-aware)."""
+    d = np.load(os.path.join(GOLD, "prologue_small.npz"))
+    n_rn = len([k for k in d.files if k.startswith("rn") and k.endswith("_y")])
+    n_sm = len([k for k in d.files if k.startswith("sm") and k.endswith("_y")])
+    assert n_rn >= 5 and n_sm >= 3
+    for i in range(n_rn):
+        p = f"rn{i}_"
+        y = oracle.rms_norm(d[p + "x"], d[p + "w"], float(d[p + "eps"]))
+        assert np.array_equal(_bits(y), _bits(d[p + "y"])), p
+    for i in range(n_sm):
+        p = f"sm{i}_"
+        y = oracle.silu_mul(d[p + "gu"])
+        assert np.array_equal(_bits(y), _bits(d[p + "y"])), p
+    # the reference tests' own expectations (backend_naive_test.cc:199-236)
+    assert np.allclose(d["rn0_y"], 1.0, atol=1e-5)
+    x1, w1 = d["rn1_x"][0], d["rn1_w"]
+    rms = np.sqrt(np.float32(14.0) / np.float32(3.0) + np.float32(1e-6))
+    assert np.allclose(d["rn1_y"][0], x1 / rms * w1, atol=1e-5)
+    # edge rows: zero row stays zero, an overflowing sum of squares gives rms = inf -> zeros
+    assert not d["rn4_y"][0].any() and not d["rn4_y"][1].any()

@@ -26,5 +26,9 @@ from ._lib import (  # noqa: F401
     linear_q8_sharded,
     linear_q8_sharded_p2p,
     quantize_per_channel,
+    rms_norm,
+    rms_norm_linear_q8,
     shard_range,
+    silu_mul,
+    silu_mul_linear_q8_add,
 )

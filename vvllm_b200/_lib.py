@@ -60,6 +60,11 @@ _SIGS = {
         [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, ctypes.c_uint, _vp], _int),
     "b200q8_comm_wait": ([_vp, _vp], _int),
     "b200q8_linear_q8_argmax": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp], _int),
+    "b200q8_rms_norm_linear_q8": (
+        [_vp, _int, _vp, _int, _vp, ctypes.c_float, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_silu_mul_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
+    "b200q8_rms_norm": ([_vp, _vp, _int, _vp, ctypes.c_float, _sz, _sz, _vp], _int),
+    "b200q8_silu_mul": ([_vp, _vp, _int, _sz, _sz, _vp], _int),
 }
 
 # Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
@@ -150,6 +155,39 @@ def linear_q8_argmax(out, x, w, scales, bias, argmax, out_dtype=None, stream=Non
     odt = _dtype_code(out) if out is not None else (F32 if out_dtype is None else out_dtype)
     _check(lib().b200q8_linear_q8_argmax(_addr(out), odt, _addr(x), _dtype_code(x), _addr(w), _addr(scales),
                                          _addr(bias), M, N, K, _addr(argmax), _stream(stream)))
+
+
+def rms_norm_linear_q8(out, x, norm_weight, eps, w, scales, bias=None, stream=None) -> None:
+    """out[M,N] = linear_q8(rms_norm(x[M,K], norm_weight[K], eps)) with the norm fused into the GEMV."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib().b200q8_rms_norm_linear_q8(_addr(out), _dtype_code(out), _addr(x), _dtype_code(x),
+                                           _addr(norm_weight), float(eps), _addr(w), _addr(scales), _addr(bias),
+                                           M, N, K, _stream(stream)))
+
+
+def silu_mul_linear_q8_add(out, gate_up, w, scales, bias=None, residual=None, stream=None) -> None:
+    """out[M,N] = linear_q8(silu(gate_up[:, :K]) * gate_up[:, K:]) (+ residual), K = w.shape[1]."""
+    M = gate_up.shape[0]
+    N, K = w.shape
+    if gate_up.shape[1] != 2 * K:
+        raise ValueError(f"gate_up must be [M, 2K] = [{M}, {2 * K}], got {tuple(gate_up.shape)}")
+    _check(lib().b200q8_silu_mul_linear_q8_add(_addr(out), _dtype_code(out), _addr(gate_up), _dtype_code(gate_up),
+                                               _addr(w), _addr(scales), _addr(bias), _addr(residual), M, N, K,
+                                               _stream(stream)))
+
+
+def rms_norm(out, x, norm_weight, eps, stream=None) -> None:
+    """out[M,K] = rms_norm(x[M,K]) per token (same arithmetic as the fused prologue)."""
+    M, K = x.shape
+    _check(lib().b200q8_rms_norm(_addr(out), _addr(x), _dtype_code(x), _addr(norm_weight), float(eps), M, K,
+                                 _stream(stream)))
+
+
+def silu_mul(out, gate_up, stream=None) -> None:
+    """out[M,K] = silu(gate_up[:, :K]) * gate_up[:, K:]."""
+    M, K2 = gate_up.shape
+    _check(lib().b200q8_silu_mul(_addr(out), _addr(gate_up), _dtype_code(gate_up), M, K2 // 2, _stream(stream)))
 
 
 ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_TC_I8 = 0, 1, 2, 3

@@ -21,6 +21,7 @@
 
 #include "b200q8.h"
 #include "kernels.h"
+#include "prologue.cuh"
 
 namespace b200q8 {
 
@@ -108,7 +109,7 @@ std::mutex g_scratch_mu;
 std::unordered_map<ScratchKey, TcScratch, ScratchKeyHash> g_scratch;
 
 struct ScratchNeed {
-    size_t ws = 0, counters = 0, dig = 0, exps = 0;
+    size_t ws = 0, counters = 0, exps = 0, act = 0;
     bool amax = false;
 };
 
@@ -144,12 +145,12 @@ int get_scratch(const ScratchNeed& need, int num_sms, cudaStream_t stream, TcScr
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     TcScratch& s = g_scratch[ScratchKey{dev, stream}];
-    // Default capacities: 128-column partials on every SM, 64K tiles, 64 tokens x 32K digits.
+    // Default capacities: 128-column partials on every SM, 64K tiles.
     int st;
     if ((st = grow(&s.ws, &s.ws_floats, need.ws, (size_t)2 * num_sms * 128 * 128, stream, false, "partials")) ||
         (st = grow(&s.counter_ptr, &s.counters, need.counters, (size_t)1 << 16, stream, true, "counters")) ||
-        (st = grow(&s.dig, &s.dig_bytes, need.dig, (size_t)4 * 64 * 32768, stream, false, "digits")) ||
-        (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)64, stream, false, "exponents")))
+        (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)320, stream, true, "exponents")) ||
+        (st = grow(&s.act, &s.act_bytes, need.act, 0, stream, false, "prologue activations")))
         return st;
     if (need.amax && !s.amax) {  // argmax keys + done counter, zero at rest
         size_t have = 0;
@@ -165,8 +166,11 @@ int reset_scratch_counters(int dev)
 {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     for (auto& kv : g_scratch) {
-        if (kv.first.dev != dev || !kv.second.counter_ptr) continue;
-        cudaError_t e = cudaMemset(kv.second.counter_ptr, 0, kv.second.counters * sizeof(int));
+        if (kv.first.dev != dev) continue;
+        cudaError_t e = cudaSuccess;
+        if (kv.second.counter_ptr) e = cudaMemset(kv.second.counter_ptr, 0, kv.second.counters * sizeof(int));
+        if (e == cudaSuccess && kv.second.exps)  // the prep kernel's zero-at-rest words live here
+            e = cudaMemset(kv.second.exps, 0, kv.second.exps_count * sizeof(int));
         if (e == cudaSuccess && kv.second.amax)
             e = cudaMemset(kv.second.amax, 0, (kMaxArgmaxTokens + 1) * sizeof(unsigned long long));
         if (e != cudaSuccess) return cuda_fail(e, "reset scratch counters");
@@ -174,9 +178,12 @@ int reset_scratch_counters(int dev)
     return B200Q8_OK;
 }
 
+// pro / norm_w / eps: an elementwise prologue (prologue.cuh) that turns inp into the activations
+// -- fused into the int8 digit GEMV, or run first into scratch when the GEMM takes the shape.
 int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
                 const float* scales, const float* bias, const void* residual, size_t M, size_t N,
-                size_t K, cudaStream_t stream, int algo = B200Q8_ALGO_AUTO)
+                size_t K, cudaStream_t stream, int algo = B200Q8_ALGO_AUTO, int pro = kProNone,
+                const float* norm_w = nullptr, float eps = 0.0f)
 {
     if (algo != B200Q8_ALGO_AUTO && algo != B200Q8_ALGO_SIMT && algo != B200Q8_ALGO_TC &&
         algo != B200Q8_ALGO_TC_I8)
@@ -191,9 +198,10 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
         N * K / K != N)
         return fail(B200Q8_ERR_INVALID, "linear_q8: sizes overflow (M=%zu N=%zu K=%zu)", M, N, K);
     const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4, ib = in_dtype == B200Q8_F16 ? 2 : 4;
+    const size_t ldx = pro == kProSiluMul ? 2 * K : K;  // input row length
     {   // inp must not overlap out
         const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
-        const uintptr_t i0 = (uintptr_t)inp, i1 = i0 + M * K * ib;
+        const uintptr_t i0 = (uintptr_t)inp, i1 = i0 + M * ldx * ib;
         if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8: inp overlaps out");
     }
     DeviceInfo d;
@@ -216,7 +224,7 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     cudaError_t e;
     // Kernel choice (AUTO): up to 16 tokens -> int8 tensor-core GEMV with exact activation digits;
     // more tokens with fp16 activations -> fp16 tensor-core GEMM (weights dequantized into TMEM);
-    // more tokens with fp32 activations -> the digit kernel in groups of up to 64 tokens.
+    // more tokens with fp32 activations -> the digit kernel in groups of up to 42 tokens.
     // Shapes the tensor-core kernels cannot take (K % 16 != 0, misaligned) use the SIMT GEMV.
     const bool tc_ok = gemm_tc_supports(a);
     LinearArgs a1 = a;
@@ -233,6 +241,22 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     const bool use_i8 = algo == B200Q8_ALGO_TC_I8 ||
                         (algo == B200Q8_ALGO_AUTO && i8_ok && (M <= 16 || !tc_ok));
     const bool use_tc = !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok));
+    if (pro != kProNone && !use_i8) {
+        // The GEMM (or SIMT) kernel reads plain activations: write them once into scratch.
+        ScratchNeed need;
+        need.act = M * K * ib;
+        TcScratch scratch;
+        if ((st = get_scratch(need, d.num_sms, stream, &scratch))) return st;
+        e = launch_prologue(pro, inp, scratch.act, in_dtype, norm_w, eps, M, K, true, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+        a.x = inp = scratch.act;
+        pro = kProNone;
+    }
+    if (pro != kProNone) {
+        a.prologue = pro;
+        a.norm_w = norm_w;
+        a.eps = eps;
+    }
     if (use_tc) {
         ScratchNeed need;
         gemm_tc_scratch_need(a, d.num_sms, &need.ws, &need.counters);
@@ -247,11 +271,11 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
         for (size_t m0 = 0; m0 < M; m0 += mt) {
             LinearArgs b = a;
             b.M = (M - m0 < mt) ? (M - m0) : mt;
-            b.x = (const char*)inp + m0 * K * ib;
+            b.x = (const char*)inp + m0 * ldx * ib;
             b.out = (char*)out + m0 * N * ob;
             b.res = residual ? (const char*)residual + m0 * N * ob : nullptr;
             ScratchNeed need;
-            gemv_i8_scratch_need(b, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+            gemv_i8_scratch_need(b, d.num_sms, &need.ws, &need.counters, &need.act, &need.exps);
             TcScratch scratch;
             if ((st = get_scratch(need, d.num_sms, stream, &scratch))) return st;
             e = launch_q8_gemv_i8(b, d.num_sms, scratch, stream);
@@ -445,7 +469,7 @@ int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dt
         return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_argmax: needs K %% 16 == 0, 16 <= K <= 131072, a 16-byte "
                                             "aligned weight and an 8-byte (fp16) / 16-byte (fp32) aligned input");
     ScratchNeed need;
-    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.act, &need.exps);
     need.amax = true;
     TcScratch scratch;
     if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
@@ -472,6 +496,95 @@ int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, int in_dtype
     }
     return linear_impl(out, out_dtype, inp, in_dtype, weight, scales, bias, residual, M, N, K,
                        (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+namespace b200q8 {
+namespace {
+
+// Shape / alignment rules shared by the prologue entry points: rows of 4-element groups,
+// fp16 rows 8-byte and fp32 rows 16-byte aligned (the prologue's vector loads).
+int check_prologue_io(const char* what, const void* x, const void* out, int dtype, size_t M, size_t K, size_t ldx)
+{
+    if (!valid_dtype(dtype)) return fail(B200Q8_ERR_INVALID, "%s: dtype must be B200Q8_F32 or B200Q8_F16", what);
+    if (!x || !out) return fail(B200Q8_ERR_INVALID, "%s: null input/output", what);
+    const size_t eb = dtype == B200Q8_F16 ? 2 : 4, al = dtype == B200Q8_F16 ? 8 : 16;
+    if (K % 4 != 0 || K > (size_t)INT32_MAX || M > (size_t)INT32_MAX)
+        return fail(B200Q8_ERR_UNSUPPORTED, "%s: needs K %% 4 == 0 (K=%zu)", what, K);
+    if ((uintptr_t)x % al || (uintptr_t)out % al)
+        return fail(B200Q8_ERR_UNSUPPORTED, "%s: input/output must be %zu-byte aligned", what, al);
+    const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * K * eb, i0 = (uintptr_t)x, i1 = i0 + M * ldx * eb;
+    if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "%s: input overlaps output", what);
+    return B200Q8_OK;
+}
+
+}  // namespace
+}  // namespace b200q8
+
+extern "C" {
+
+int b200q8_rms_norm(void* out, const void* x, int dtype, const float* norm_weight, float eps, size_t M, size_t K,
+                    b200q8_stream_t stream)
+{
+    if (M == 0 || K == 0) return B200Q8_OK;
+    int st = check_prologue_io("rms_norm", x, out, dtype, M, K, K);
+    if (st) return st;
+    if (!norm_weight) return fail(B200Q8_ERR_INVALID, "rms_norm: null norm_weight");
+    if ((uintptr_t)norm_weight % 16) return fail(B200Q8_ERR_UNSUPPORTED, "rms_norm: norm_weight must be 16-byte aligned");
+    const cudaError_t e = launch_prologue(kProRmsNorm, x, out, dtype, norm_weight, eps, M, K, true, (cudaStream_t)stream);
+    return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "rms_norm launch");
+}
+
+int b200q8_silu_mul(void* out, const void* gate_up, int dtype, size_t M, size_t K, b200q8_stream_t stream)
+{
+    if (M == 0 || K == 0) return B200Q8_OK;
+    int st = check_prologue_io("silu_mul", gate_up, out, dtype, M, K, 2 * K);
+    if (st) return st;
+    const cudaError_t e = launch_prologue(kProSiluMul, gate_up, out, dtype, nullptr, 0.0f, M, K, true,
+                                          (cudaStream_t)stream);
+    return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "silu_mul launch");
+}
+
+int b200q8_rms_norm_linear_q8(void* out, int out_dtype, const void* x, int in_dtype, const float* norm_weight,
+                              float eps, const int8_t* weight, const float* scales, const float* bias, size_t M,
+                              size_t N, size_t K, b200q8_stream_t stream)
+{
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!valid_dtype(in_dtype)) return fail(B200Q8_ERR_INVALID, "rms_norm_linear_q8: bad in_dtype");
+    if (!norm_weight) return fail(B200Q8_ERR_INVALID, "rms_norm_linear_q8: null norm_weight");
+    if ((uintptr_t)norm_weight % 16)
+        return fail(B200Q8_ERR_UNSUPPORTED, "rms_norm_linear_q8: norm_weight must be 16-byte aligned");
+    if (!x) return fail(B200Q8_ERR_INVALID, "rms_norm_linear_q8: null x");
+    const size_t al = in_dtype == B200Q8_F16 ? 8 : 16;
+    if (K % 4 != 0 || (uintptr_t)x % al)
+        return fail(B200Q8_ERR_UNSUPPORTED, "rms_norm_linear_q8: needs K %% 4 == 0 and a %zu-byte aligned x (K=%zu)",
+                    al, K);
+    return linear_impl(out, out_dtype, x, in_dtype, weight, scales, bias, nullptr, M, N, K, (cudaStream_t)stream,
+                       B200Q8_ALGO_AUTO, kProRmsNorm, norm_weight, eps);
+}
+
+int b200q8_silu_mul_linear_q8_add(void* out, int out_dtype, const void* gate_up, int in_dtype,
+                                  const int8_t* weight, const float* scales, const float* bias, const void* residual,
+                                  size_t M, size_t N, size_t K, b200q8_stream_t stream)
+{
+    if (M == 0 || N == 0) return B200Q8_OK;
+    if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype))
+        return fail(B200Q8_ERR_INVALID, "silu_mul_linear_q8_add: dtype must be B200Q8_F32 or B200Q8_F16");
+    if (!gate_up) return fail(B200Q8_ERR_INVALID, "silu_mul_linear_q8_add: null gate_up");
+    const size_t al = in_dtype == B200Q8_F16 ? 8 : 16;
+    if (K % 4 != 0 || (uintptr_t)gate_up % al)
+        return fail(B200Q8_ERR_UNSUPPORTED,
+                    "silu_mul_linear_q8_add: needs K %% 4 == 0 and a %zu-byte aligned gate_up (K=%zu)", al, K);
+    if (residual && residual != out) {  // residual must either be out itself or not overlap it
+        const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4;
+        const uintptr_t o0 = (uintptr_t)out, o1 = o0 + M * N * ob;
+        const uintptr_t r0 = (uintptr_t)residual, r1 = r0 + M * N * ob;
+        if (o0 < r1 && r0 < o1)
+            return fail(B200Q8_ERR_INVALID, "silu_mul_linear_q8_add: residual partially overlaps out");
+    }
+    return linear_impl(out, out_dtype, gate_up, in_dtype, weight, scales, bias, residual, M, N, K,
+                       (cudaStream_t)stream, B200Q8_ALGO_AUTO, kProSiluMul);
 }
 
 }  // extern "C"
@@ -1027,7 +1140,7 @@ int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, co
         return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_sharded_p2p: needs K %% 16 == 0, 16 <= K <= 131072 and "
                                             "aligned pointers (K=%zu)", K);
     ScratchNeed need;
-    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.dig, &need.exps);
+    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.act, &need.exps);
     TcScratch scratch;
     if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
     // A deferred wait of the previous call is owed before this call reads its input: it is paid

@@ -51,6 +51,12 @@ struct LinearArgs {
     unsigned long long* amax_keys = nullptr;
     unsigned int* amax_done = nullptr;
     int* amax_out = nullptr;
+    // int8 digit GEMV only: an elementwise prologue computed from x where the GEMV reads its
+    // activations (prologue.cuh; kProNone: x is the activation).  x is then the prologue's
+    // input: [M, K] for kProRmsNorm (norm_w [K], eps), [M, 2K] gate | up for kProSiluMul.
+    int prologue = 0;
+    const float* norm_w = nullptr;
+    float eps = 0.0f;
 };
 
 // One thread waits (bounded, `timeout_ns`) until counts[j] has reached seq << kCountShift for
@@ -77,15 +83,15 @@ struct TcScratch {
     size_t ws_floats = 0;
     int* counter_ptr = nullptr;  // per-tile arrival counters
     size_t counters = 0;
-    int8_t* dig = nullptr;       // activation digits [4M, K] (int8 digit GEMV)
-    size_t dig_bytes = 0;
-    int* exps = nullptr;         // per-token exponents [M]
+    int* exps = nullptr;         // per-token exponents [M], then the tokens' rms [M] (fp32 bits)
     size_t exps_count = 0;
+    unsigned char* act = nullptr;  // activations a prologue wrote for the following GEMV / GEMM
+    size_t act_bytes = 0;
     unsigned long long* amax = nullptr;  // argmax keys [kMaxArgmaxTokens] + a counter word, zero at rest
 };
 constexpr int kMaxArgmaxTokens = 64;
 
-// Tensor-core GEMV for M <= gemv_i8_max_tokens() with exact 4-digit int8
+// Tensor-core GEMV for M <= gemv_i8_max_tokens() with exact 6-digit int8
 // activations (fp16 or fp32 inputs) and kind::i8 MMAs on the raw int8 weights.
 cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream);
 bool gemv_i8_supports(const LinearArgs& a);
@@ -93,7 +99,7 @@ bool gemv_i8_supports(const LinearArgs& a);
 // so a deferred peer wait can happen inside it).
 bool gemv_i8_fused_exps(const LinearArgs& a);
 int gemv_i8_max_tokens();
-void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* dig_bytes,
+void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* act_bytes,
                           size_t* exps);
 cudaError_t read_kernel_error_i8(int* code, bool clear);
 
@@ -116,6 +122,12 @@ cudaError_t read_kernel_error(int* code, bool clear);
 // [G][M][Ns] (rank-major gather result) -> [M][N] (N = true width, Ns = padded shard width)
 cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, size_t G, size_t M,
                                   size_t Ns, size_t N, cudaStream_t stream);
+
+// Standalone prologue (prologue.cuh) over M tokens: out[M, K] in `dtype` from x ([M, K] for
+// kProRmsNorm, [M, 2K] for kProSiluMul).  K % 4 == 0; x and out 8-byte (fp16) / 16-byte (fp32)
+// aligned.  Same arithmetic as the prologue fused into the digit GEMV.
+cudaError_t launch_prologue(int pro, const void* x, void* out, int dtype, const float* norm_w, float eps, size_t M,
+                            size_t K, bool pdl, cudaStream_t stream);
 
 // Counts every kernel launch made by this library (for the bench's launch count).
 void note_launch();

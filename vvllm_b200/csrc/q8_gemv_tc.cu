@@ -47,6 +47,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "prologue.cuh"
 #include "sk_common.cuh"
 #include "tc_utils.cuh"
 #include "tmap.cuh"
@@ -65,10 +66,18 @@ constexpr int kDigits = 6;
 constexpr int kF16Exp = 24;  // 2^24 * fp16 is an integer for every finite fp16
 constexpr int kQBits = 40;   // |x_q| < 2^40
 constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
+constexpr int kPrepWords = 3 * kMaxTokens;  // the prep kernel's combine words, ahead of the exponents
 // Up to this many tokens of at most this length, every CTA scans x for the exponents itself
 // (saves the prep kernel's launch); longer rows would delay the first digits more than that.
 constexpr int kFusedExpTokens = 4;
 constexpr size_t kFusedExpMaxK = 4096;
+// With a prologue and few tokens, the in-kernel scan also computes the activations where the
+// digitizers read them, for weights up to this size; above it, and beyond the in-kernel scan's
+// limits, the prep kernel writes them once to scratch and the GEMV reads them as plain x.
+// Measured on B200 (one fp16 token): Qwen2.5-0.5B gate_up (9.7 MB) +0.9 us in-kernel vs +1.9 us
+// through the prep kernel; Qwen2-7B gate_up (136 MB) +2.3 us vs +1.2 us (the prep kernel runs
+// while the GEMV's first weight stages load; the in-kernel scan delays the digits).
+constexpr size_t kPrologueInKernelMaxBytes = (size_t)32 << 20;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 constexpr uint64_t kPeerTimeoutNs = 2000000000ull;  // a peer's flag of the previous gathered call
 
@@ -91,6 +100,12 @@ struct DigParams {
     unsigned long long* amax_keys;  // [M]
     unsigned int* amax_done;        // CTAs finished, zero between launches
     int* amax_out;                  // [M] result
+    // Prologue (prologue.cuh) applied where the digitizers read x; x rows are ldx apart.
+    int pro;
+    const float* norm_w;
+    float eps;
+    long long ldx;
+    const float* rms;  // [M] the prep kernel's per-token rms (kProRmsNorm without fused exponents)
 };
 
 template <int NC, int BK, int S>
@@ -105,7 +120,8 @@ struct DigCfg {
                                      : kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kNumBars = 3 * S + 4 + 1;  // full, dfull, empty per stage; acc x4; drain
     static constexpr int kSmemBytes =
-        1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 32 + 8 * kMaxTokens + 8;
+        1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 64 + 8 * kMaxTokens + 8 + 64 +
+        4 * kMaxTokens;
     static_assert(NC % 16 == 0 && NC >= 16 && NC <= 256, "kind::i8 N for M=128");
     static_assert(BK % 128 == 0, "whole 128-byte boxes");
     static_assert(kColsNeeded <= 512, "TMEM overflow");
@@ -138,60 +154,181 @@ __device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsign
 }
 
 // ----------------------------------------------------------------------------- prep
-// One CTA per token: the exponent e (fp16: 24; fp32: 39 - floor(log2(max|x|))) or
-// INT_MIN when the row holds Inf/NaN.
+// max |a| over the 4-element groups [c0, c1) of one token's row taken by thread t of nt, and
+// whether any a is Inf/NaN; a is x or, with a prologue, the activations it makes from x, which
+// are also stored to act_row when it is given.
 template <typename XT>
-__global__ void __launch_bounds__(1024) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps,
-                                                    const unsigned long long* wait_counts, int wait_n,
-                                                    unsigned int wait_seq)
+__device__ __forceinline__ void scan_groups(int pro, const XT* xrow, int K, const float* norm_w, float rms, int c0,
+                                            int c1, int t, int nt, float& mx, int& bad, XT* act_row = nullptr)
 {
-    pdl_launch_dependents();  // the GEMV may start streaming weights right away
-    pdl_wait();               // x is written by the previous kernel
-    __shared__ float red[32];
-    __shared__ int bad_any;
-    const int m = blockIdx.x;
-    if (threadIdx.x == 0) {
-        bad_any = 0;
-        // x is the gathered output of a deferred call: every rank's part must have landed
-        if (wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, kPeerTimeoutNs))
-            atomicOr(&g_kernel_error_i8, 2);
-    }
-    __syncthreads();
-    float mx = 0.0f;
-    int bad = 0;
-    if (sizeof(XT) == 2) {
-        // 8-byte loads: fp16 activations are only required to be 8-byte aligned
-        const uint2* xr = reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(x) + (size_t)m * K);
-        for (int i = threadIdx.x; i < (K >> 2); i += blockDim.x) {
+    if (pro != kProNone) {
+        for (int i0 = c0 + t; i0 < c1; i0 += kRowBatch * nt) {
+            float v[kRowBatch][4], aux[kRowBatch][4];
+#pragma unroll
+            for (int b = 0; b < kRowBatch; b++)  // every load of the batch first
+                if (i0 + b * nt < c1) act4_load<XT>(pro, xrow, K, 4 * (i0 + b * nt), norm_w, v[b], aux[b]);
+#pragma unroll
+            for (int b = 0; b < kRowBatch; b++) {
+                const int i = i0 + b * nt;
+                if (i >= c1) break;
+                act4_apply<XT>(pro, rms, v[b], aux[b]);
+                if (act_row) store4<XT>(act_row + 4 * i, v[b]);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {  // NaN and Inf fail a <= FLT_MAX
+                    const float a = fabsf(v[b][j]);
+                    bad |= (a <= FLT_MAX) ? 0 : 1;
+                    mx = (a <= FLT_MAX) ? fmaxf(mx, a) : mx;
+                }
+            }
+        }
+    } else if (sizeof(XT) == 2) {
+        // 8-byte loads: fp16 activations are only required to be 8-byte aligned; the exponent
+        // is fixed, only Inf/NaN (exponent field all ones) matter
+        const uint2* xr = reinterpret_cast<const uint2*>(xrow);
+        for (int i = c0 + t; i < c1; i += nt) {
             const uint2 v = xr[i];
             const uint32_t w[2] = {v.x, v.y};
 #pragma unroll
-            for (int j = 0; j < 2; j++)  // exponent field all ones: Inf or NaN
-                if (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) bad = 1;
+            for (int j = 0; j < 2; j++)
+                bad |= (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) ? 1 : 0;
         }
     } else {
-        const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + (size_t)m * K);
-        for (int i = threadIdx.x; i < (K >> 2); i += blockDim.x) {
+        const float4* xr = reinterpret_cast<const float4*>(xrow);
+        for (int i = c0 + t; i < c1; i += nt) {
             const float4 v = xr[i];
             const float a[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                if (a[j] <= FLT_MAX) mx = fmaxf(mx, a[j]); else bad = 1;  // NaN and Inf fail a <= FLT_MAX
+                bad |= (a[j] <= FLT_MAX) ? 0 : 1;
+                mx = (a[j] <= FLT_MAX) ? fmaxf(mx, a[j]) : mx;
             }
         }
     }
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    if (bad) atomicOr(&bad_any, 1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+}
+
+// The token's exponent: fp16 e = 24; fp32 e = 39 - floor(log2 max|a|); INT_MIN if any Inf/NaN.
+template <typename XT>
+__device__ __forceinline__ int token_exp(float m_all, int bad)
+{
+    if (bad) return INT_MIN;
+    if (sizeof(XT) == 2) return kF16Exp;
+    return (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
+}
+
+// Grid (M tokens, row_splits(K) CTAs per token), 256 threads: each token's exponent (and, for
+// kProRmsNorm, its rms).  With a prologue and act_out, the activations are written to act_out
+// [M, K] as well, and the GEMV behind reads them as its x.  With several CTAs per token, each folds its max / Inf-NaN flag into
+// part = [max bits][bad][arrivals], kMaxTokens words each at fixed offsets (zero at rest,
+// whatever M the previous call had), and the last to arrive writes the exponent and re-zeroes
+// its words.  256-thread CTAs fit beside a GEMV CTA on one SM, so the
+// GEMV launched behind this kernel keeps all its CTAs resident.
+template <typename XT>
+__global__ void __launch_bounds__(kSqThreads) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps,
+                                                          const unsigned long long* wait_counts, int wait_n,
+                                                          unsigned int wait_seq, int pro, const float* norm_w,
+                                                          float eps, float* __restrict__ rms_out, int* part,
+                                                          XT* __restrict__ act_out)
+{
+    pdl_launch_dependents();  // the GEMV may start streaming weights right away
+    pdl_wait();               // x is written by the previous kernel
+    __shared__ float red[kSqWarps];
+    __shared__ int bad_w[kSqWarps];
+    __shared__ double sq[kSqWarps];
+    const int m = blockIdx.x;
+    const int sp = blockIdx.y, ns = gridDim.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // x is the gathered output of a deferred call: every rank's part must have landed
+    if (tid == 0 && wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, kPeerTimeoutNs))
+        atomicOr(&g_kernel_error_i8, 2);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float m_all = 0.0f;
-        for (int i = 0; i < (int)(blockDim.x >> 5); i++) m_all = fmaxf(m_all, red[i]);
-        int e;
-        if (bad_any) e = INT_MIN;
-        else if (sizeof(XT) == 2) e = kF16Exp;
-        else e = (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
-        exps[m] = e;
+    const XT* xrow = x + (size_t)m * (pro == kProSiluMul ? 2 * (size_t)K : (size_t)K);
+    float rms = 1.0f;
+    if (pro == kProRmsNorm) {  // every CTA of the token takes the whole (fixed-order) sum
+        const double w = sumsq_warp<XT>(xrow, K, tid);
+        if (lane == 0) sq[warp] = w;
+        __syncthreads();
+        rms = rms_from(sq, K, eps);
+        if (sp == 0 && tid == 0) rms_out[m] = rms;
+    }
+    const int g4 = K >> 2;
+    const int c0 = (int)((long long)g4 * sp / ns), c1 = (int)((long long)g4 * (sp + 1) / ns);
+    float mx = 0.0f;
+    int bad = 0;
+    scan_groups<XT>(pro, xrow, K, norm_w, rms, c0, c1, tid, kSqThreads, mx, bad,
+                    act_out ? act_out + (size_t)m * K : nullptr);
+    if (lane == 0) {
+        red[warp] = mx;
+        bad_w[warp] = bad;
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    float m_all = 0.0f;
+    int b_all = 0;
+    for (int w = 0; w < kSqWarps; w++) {
+        m_all = fmaxf(m_all, red[w]);
+        b_all |= bad_w[w];
+    }
+    if (ns == 1) {
+        exps[m] = token_exp<XT>(m_all, b_all);
+        return;
+    }
+    int* pmax = part;
+    int* pbad = part + kMaxTokens;
+    unsigned int* pcnt = reinterpret_cast<unsigned int*>(part + 2 * kMaxTokens);
+    atomicMax(pmax + m, __float_as_int(m_all));  // m_all >= 0 and finite: int order is float order
+    if (b_all) atomicOr(pbad + m, 1);
+    __threadfence();
+    if (atomicAdd(pcnt + m, 1u) == (unsigned int)ns - 1) {
+        __threadfence();
+        const float mm = __int_as_float(atomicExch(pmax + m, 0));
+        const int bb = atomicExch(pbad + m, 0);
+        atomicExch(pcnt + m, 0u);
+        exps[m] = token_exp<XT>(mm, bb);
+    }
+}
+
+// The exponents (and rms) of a few tokens, computed inside the GEMV by its epilogue and
+// digitizer warps together (sid 0..255, named barrier 3), with the prep kernel's rules and the
+// same fixed-order sum of squares.
+template <typename XT>
+__device__ __forceinline__ void fused_scan(const DigParams& p, int sid, int* s_exps, float* s_rms, float* s_red,
+                                           double* s_sq)
+{
+    const int sw = sid >> 5, lane = sid & 31;
+#pragma unroll 1
+    for (int m = 0; m < p.M; m++) {
+        const XT* xrow = reinterpret_cast<const XT*>(p.x) + (size_t)m * p.ldx;
+        float rms = 1.0f;
+        if (p.pro == kProRmsNorm) {
+            const double w = sumsq_warp<XT>(xrow, p.K, sid);
+            if (lane == 0) s_sq[sw] = w;
+            asm volatile("bar.sync 3, 256;" ::: "memory");
+            rms = rms_from(s_sq, p.K, p.eps);
+            if (sid == 0) s_rms[m] = rms;
+        }
+        float mx = 0.0f;
+        int bad = 0;
+        scan_groups<XT>(p.pro, xrow, p.K, p.norm_w, rms, 0, p.K >> 2, sid, kSqThreads, mx, bad);
+        if (lane == 0) {
+            s_red[sw] = mx;
+            s_red[kSqWarps + sw] = __int_as_float(bad);
+        }
+        asm volatile("bar.sync 3, 256;" ::: "memory");
+        if (sid == 0) {
+            float m_all = 0.0f;
+            int b_all = 0;
+            for (int i = 0; i < kSqWarps; i++) {
+                m_all = fmaxf(m_all, s_red[i]);
+                b_all |= __float_as_int(s_red[kSqWarps + i]);
+            }
+            s_exps[m] = token_exp<XT>(m_all, b_all);
+        }
+        asm volatile("bar.sync 3, 256;" ::: "memory");
     }
 }
 
@@ -260,9 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
     volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]
     int* s_exps = reinterpret_cast<int*>(tmem_holder + 4);                          // [kMaxTokens]
-    float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [8] exponent reduction
+    float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [16] exponent reduction
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(                 // [kMaxTokens] argmax keys
-        (reinterpret_cast<uintptr_t>(s_red + 8) + 7) & ~static_cast<uintptr_t>(7));
+        (reinterpret_cast<uintptr_t>(s_red + 2 * kSqWarps) + 7) & ~static_cast<uintptr_t>(7));
+    double* s_sq = reinterpret_cast<double*>(s_best + kMaxTokens);                      // [8] sum-of-squares partials
+    float* s_rms = reinterpret_cast<float*>(s_sq + kSqWarps);                               // [kMaxTokens] rms per token
 
     const uint32_t bar0 = tc::smem_u32(bars);
     const uint32_t full0 = bar0, dfull0 = bar0 + 8u * S, empty0 = bar0 + 16u * S, accfull0 = bar0 + 24u * S,
@@ -389,71 +528,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ digitizers
         const int dtid = threadIdx.x - kFirstDig * 32;  // 0..127
         pdl_wait();  // x (and the prep kernel's exponents) are ready
-        if (p.po.wait_seq) {
-            // x is the gathered output of the previous call: wait until every rank's part landed
-            if (dtid == 0 && !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq, kPeerTimeoutNs)) {
-                atomicOr(&g_kernel_error_i8, 2);
-                raise_error(abort);
-            }
-            asm volatile("bar.sync 2, 128;" ::: "memory");
-        }
-        if (p.fused_exps) {
-            // Few tokens: every CTA finds the per-token exponents itself (the prep kernel's
-            // rule: fp16 e = 24; fp32 e = 39 - floor(log2 max|x|); INT_MIN if any Inf/NaN).
-            const int wd = dtid >> 5;
-#pragma unroll 1
-            for (int m = 0; m < p.M; m++) {
-                float mx = 0.0f;
-                int bad = 0;
-                if (sizeof(XT) == 2) {
-                    // 8-byte loads: fp16 activations need only 8-byte alignment on this path
-                    const uint2* xr = reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.x) + (size_t)m * p.K);
-                    for (int i = dtid; i < (p.K >> 2); i += 128) {
-                        const uint2 v = xr[i];
-                        const uint32_t w[2] = {v.x, v.y};
-#pragma unroll
-                        for (int j = 0; j < 2; j++)  // exponent field all ones: Inf or NaN
-                            bad |= (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) ? 1 : 0;
-                    }
-                } else {
-                    const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (size_t)m * p.K);
-                    for (int i = dtid; i < (p.K >> 2); i += 128) {
-                        const float4 v = xr[i];
-                        const float a[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {  // NaN and Inf fail a <= FLT_MAX
-                            bad |= (a[j] <= FLT_MAX) ? 0 : 1;
-                            mx = (a[j] <= FLT_MAX) ? fmaxf(mx, a[j]) : mx;
-                        }
-                    }
-                }
-                for (int o = 16; o > 0; o >>= 1) {
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-                }
-                if (lane == 0) {
-                    s_red[wd] = mx;
-                    s_red[4 + wd] = __int_as_float(bad);
-                }
-                asm volatile("bar.sync 2, 128;" ::: "memory");
-                if (dtid == 0) {
-                    float m_all = 0.0f;
-                    int b_all = 0;
-                    for (int i = 0; i < 4; i++) {
-                        m_all = fmaxf(m_all, s_red[i]);
-                        b_all |= __float_as_int(s_red[4 + i]);
-                    }
-                    int e;
-                    if (b_all) e = INT_MIN;
-                    else if (sizeof(XT) == 2) e = kF16Exp;
-                    else e = (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
-                    s_exps[m] = e;
-                }
-                asm volatile("bar.sync 2, 128;" ::: "memory");
-            }
+        // x is the gathered output of the previous call: wait until every rank's part landed
+        if (p.po.wait_seq && dtid == 0 &&
+            !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq, kPeerTimeoutNs)) {
+            atomicOr(&g_kernel_error_i8, 2);
+            raise_error(abort);
         }
         if (p.fused_exps || p.po.wait_seq)
-            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents / peers' outputs ready for the epilogue
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed (the epilogue reads them too)
+        // Few tokens: the epilogue and digitizer warps find the per-token exponents themselves.
+        if (p.fused_exps) fused_scan<XT>(p, 128 + dtid, s_exps, s_rms, s_red, s_sq);
         const int* exps = p.fused_exps ? s_exps : p.exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
@@ -477,15 +561,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
                     if (k < p.K && e != INT_MIN) {
                         float v[4];
-                        if (sizeof(XT) == 2) {
-                            const uint2 raw = *reinterpret_cast<const uint2*>(xg + (size_t)m * p.K + k);
-                            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                            v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
-                        } else {
-                            const float4 raw = *reinterpret_cast<const float4*>(xg + (size_t)m * p.K + k);
-                            v[0] = raw.x; v[1] = raw.y; v[2] = raw.z; v[3] = raw.w;
-                        }
+                        const float rms = p.pro == kProRmsNorm ? (p.fused_exps ? s_rms[m] : p.rms[m]) : 1.0f;
+                        act4<XT>(p.pro, xg + (size_t)m * p.ldx, p.K, k, p.norm_w, rms, v);
 #pragma unroll
                         for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
                     }
@@ -513,7 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         if (p.fused_exps || p.po.wait_seq)
-            asm volatile("bar.sync 3, 256;" ::: "memory");  // exponents / peers' outputs ready
+            asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed
+        if (p.fused_exps) fused_scan<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_rms, s_red, s_sq);
         if (!p.fused_exps) {
             if (threadIdx.x - kFirstEpi * 32 < p.M) s_exps[threadIdx.x - kFirstEpi * 32] = p.exps[threadIdx.x - kFirstEpi * 32];
             asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -809,11 +887,18 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.bias = a.bias;
     p.res = a.res;
     p.out = a.out;
-    p.exps = sc.exps;
+    // exps scratch: [prep kernel's zero-at-rest words 3 * kMaxTokens][exps M][rms M]
+    int* const exps_base = sc.exps + kPrepWords;
+    p.exps = exps_base;
     p.fused_exps = gemv_i8_fused_exps(a) ? 1 : 0;
     p.amax_keys = a.amax_keys;
     p.amax_done = a.amax_done;
     p.amax_out = a.amax_out;
+    p.pro = a.prologue;
+    p.norm_w = a.norm_w;
+    p.eps = a.eps;
+    p.ldx = a.prologue == kProSiluMul ? 2 * (long long)a.K : (long long)a.K;
+    p.rms = reinterpret_cast<const float*>(exps_base + a.M);
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -835,13 +920,23 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     const unsigned int prep_wait_seq = p.fused_exps ? 0u : p.po.wait_seq;
     if (!p.fused_exps) p.po.wait_seq = 0;
     const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
+    // A prologue without in-kernel exponents: the prep kernel writes the activations, the GEMV
+    // reads them as plain x.
+    const bool materialize = a.prologue != kProNone && !p.fused_exps;
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
-        sc.exps_count < a.M)
+        sc.exps_count < kPrepWords + 2 * a.M || (materialize && sc.act_bytes < a.M * a.K * sizeof(XT)))
         return cudaErrorMemoryAllocation;
+    if (materialize) {
+        p.x = sc.act;
+        p.pro = kProNone;
+        p.ldx = (long long)a.K;
+    }
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
-    e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M), dim3(1024), 0, stream, a.pdl,
-                  reinterpret_cast<const XT*>(a.x), (int)a.K, sc.exps, p.po.wait_counts, p.po.wait_n, prep_wait_seq);
+    e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)row_splits((long long)a.K)), dim3(kSqThreads), 0,
+                  stream, a.pdl, reinterpret_cast<const XT*>(a.x), (int)a.K, exps_base, p.po.wait_counts,
+                  p.po.wait_n, prep_wait_seq, a.prologue, a.norm_w, a.eps, reinterpret_cast<float*>(exps_base + a.M),
+                  sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
     if (e != cudaSuccess) return e;
     return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
 }
@@ -862,7 +957,11 @@ cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& sc, 
 
 int gemv_i8_max_tokens() { return kMaxTokens; }
 
-bool gemv_i8_fused_exps(const LinearArgs& a) { return a.M <= (size_t)kFusedExpTokens && a.K <= kFusedExpMaxK; }
+bool gemv_i8_fused_exps(const LinearArgs& a)
+{
+    return a.M <= (size_t)kFusedExpTokens && a.K <= kFusedExpMaxK &&
+           (a.prologue == kProNone || a.N * a.K <= kPrologueInKernelMaxBytes);
+}
 
 bool gemv_i8_supports(const LinearArgs& a)
 {
@@ -872,7 +971,7 @@ bool gemv_i8_supports(const LinearArgs& a)
            encode_fn() != nullptr;
 }
 
-void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* dig_bytes,
+void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* act_bytes,
                           size_t* exps)
 {
     const int NC = pick_nc(a.M);
@@ -881,8 +980,9 @@ void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, s
     const long long G = pick_grid_i8(tiles, (long long)((a.K + BK - 1) / BK), (long long)a.N * (long long)a.K, num_sms);
     *ws_floats = (size_t)(2 * G * NC * kTileRows);
     *counters = (size_t)tiles;
-    *dig_bytes = 0;
-    *exps = a.M;
+    // the prologue's activations, when the prep kernel writes them for the GEMV
+    *act_bytes = (a.prologue != kProNone && !gemv_i8_fused_exps(a)) ? a.M * a.K * (a.in_dtype == kF16 ? 2 : 4) : 0;
+    *exps = kPrepWords + 2 * a.M;  // the prep kernel's zero-at-rest words, exponents, the prologue's rms
 }
 
 cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& sc, cudaStream_t stream)
@@ -930,7 +1030,7 @@ constexpr int kNoAllocMaxTokens = 2;      // 6 digit rows per token: NC = 16
 constexpr int kNoAllocMaxCtas = 160;      // stream-K CTAs (a B200 has 148 SMs)
 constexpr int kNoAllocMaxTiles = 4096;    // 128-row tiles: N <= 524288
 constexpr size_t kNoAllocPartialInts = (size_t)2 * kNoAllocMaxCtas * kTileRows * 16;
-constexpr size_t kNoAllocExps = 64;
+constexpr size_t kNoAllocExps = 256;  // kPrepWords + exponents + rms
 constexpr size_t kNoAllocBytes = (kNoAllocPartialInts + kNoAllocMaxTiles + kNoAllocExps) * sizeof(int);
 
 }  // namespace
