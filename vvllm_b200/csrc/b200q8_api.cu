@@ -149,7 +149,7 @@ int get_scratch(const ScratchNeed& need, int num_sms, cudaStream_t stream, TcScr
     int st;
     if ((st = grow(&s.ws, &s.ws_floats, need.ws, (size_t)2 * num_sms * 128 * 128, stream, false, "partials")) ||
         (st = grow(&s.counter_ptr, &s.counters, need.counters, (size_t)1 << 16, stream, true, "counters")) ||
-        (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)320, stream, true, "exponents")) ||
+        (st = grow(&s.exps, &s.exps_count, need.exps, (size_t)320, stream, false, "exponent words")) ||
         (st = grow(&s.act, &s.act_bytes, need.act, 0, stream, false, "prologue activations")))
         return st;
     if (need.amax && !s.amax) {  // argmax keys + done counter, zero at rest
@@ -169,8 +169,6 @@ int reset_scratch_counters(int dev)
         if (kv.first.dev != dev) continue;
         cudaError_t e = cudaSuccess;
         if (kv.second.counter_ptr) e = cudaMemset(kv.second.counter_ptr, 0, kv.second.counters * sizeof(int));
-        if (e == cudaSuccess && kv.second.exps)  // the prep kernel's zero-at-rest words live here
-            e = cudaMemset(kv.second.exps, 0, kv.second.exps_count * sizeof(int));
         if (e == cudaSuccess && kv.second.amax)
             e = cudaMemset(kv.second.amax, 0, (kMaxArgmaxTokens + 1) * sizeof(unsigned long long));
         if (e != cudaSuccess) return cuda_fail(e, "reset scratch counters");

@@ -83,7 +83,7 @@ struct TcScratch {
     size_t ws_floats = 0;
     int* counter_ptr = nullptr;  // per-tile arrival counters
     size_t counters = 0;
-    int* exps = nullptr;         // per-token exponents [M], then the tokens' rms [M] (fp32 bits)
+    int* exps = nullptr;         // the digit GEMV's prep kernel words [M][row splits]
     size_t exps_count = 0;
     unsigned char* act = nullptr;  // activations a prologue wrote for the following GEMV / GEMM
     size_t act_bytes = 0;

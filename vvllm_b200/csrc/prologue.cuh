@@ -110,26 +110,29 @@ __device__ __forceinline__ void act4(int pro, const XT* xrow, int K, int k, cons
 }
 
 // Groups of a row handled per batch by one thread: all their loads are issued before any
-// arithmetic, so a thread waits for memory once per batch rather than once per group.
+// arithmetic, so a thread waits for memory once per batch rather than once per group.  Passes
+// holding two operands per group in callers short of registers (the GEMV's warps, the prep
+// kernel that must fit beside a GEMV CTA) use 2.
 constexpr int kRowBatch = 4;
 
 // Thread t (0..kSqThreads-1) of the token's sum of squares: its double partial over 4-element
 // groups t, t+kSqThreads, ..., reduced over its warp (every lane gets the warp's sum).  K % 4 == 0.
-template <typename XT>
+// (The batch size B changes only when loads are issued, not the order of the sum.)
+template <typename XT, int B = kRowBatch>
 __device__ __forceinline__ double sumsq_warp(const XT* xrow, int K, int t)
 {
     double s = 0.0;
     const int g4 = K >> 2;
-    for (int i0 = t; i0 < g4; i0 += kRowBatch * kSqThreads) {
-        float v[kRowBatch][4];
+    for (int i0 = t; i0 < g4; i0 += B * kSqThreads) {
+        float v[B][4];
 #pragma unroll
-        for (int b = 0; b < kRowBatch; b++) {
+        for (int b = 0; b < B; b++) {
             const int i = i0 + b * kSqThreads;
             if (i < g4) load4<XT>(xrow + 4 * i, v[b]);
             else v[b][0] = v[b][1] = v[b][2] = v[b][3] = 0.0f;
         }
 #pragma unroll
-        for (int b = 0; b < kRowBatch; b++)  // groups in order t, t+256, ...: the fixed order
+        for (int b = 0; b < B; b++)  // groups in order t, t+256, ...: the fixed order
 #pragma unroll
             for (int j = 0; j < 4; j++) s += (double)v[b][j] * (double)v[b][j];  // exact products
     }

@@ -66,7 +66,6 @@ constexpr int kDigits = 6;
 constexpr int kF16Exp = 24;  // 2^24 * fp16 is an integer for every finite fp16
 constexpr int kQBits = 40;   // |x_q| < 2^40
 constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
-constexpr int kPrepWords = 3 * kMaxTokens;  // the prep kernel's combine words, ahead of the exponents
 // Up to this many tokens of at most this length, every CTA scans x for the exponents itself
 // (saves the prep kernel's launch); longer rows would delay the first digits more than that.
 constexpr int kFusedExpTokens = 4;
@@ -87,7 +86,8 @@ struct DigParams {
     const float* bias;
     const void* res;
     void* out;
-    const int* exps;  // [M] exponent per token (INT_MIN: the row holds Inf/NaN)
+    const int* prep_part;  // [M][prep_splits] the prep kernel's words (without in-kernel exponents)
+    int prep_splits;
     int* ws;          // [2 * gridDim.x][128][NC] int32 partial digit sums
     int* counters;    // [tiles] arrival counters, zero between launches
     int M, N, K;
@@ -105,7 +105,6 @@ struct DigParams {
     const float* norm_w;
     float eps;
     long long ldx;
-    const float* rms;  // [M] the prep kernel's per-token rms (kProRmsNorm without fused exponents)
 };
 
 template <int NC, int BK, int S>
@@ -157,18 +156,18 @@ __device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsign
 // max |a| over the 4-element groups [c0, c1) of one token's row taken by thread t of nt, and
 // whether any a is Inf/NaN; a is x or, with a prologue, the activations it makes from x, which
 // are also stored to act_row when it is given.
-template <typename XT>
+template <typename XT, int B>
 __device__ __forceinline__ void scan_groups(int pro, const XT* xrow, int K, const float* norm_w, float rms, int c0,
                                             int c1, int t, int nt, float& mx, int& bad, XT* act_row = nullptr)
 {
     if (pro != kProNone) {
-        for (int i0 = c0 + t; i0 < c1; i0 += kRowBatch * nt) {
-            float v[kRowBatch][4], aux[kRowBatch][4];
+        for (int i0 = c0 + t; i0 < c1; i0 += B * nt) {
+            float v[B][4], aux[B][4];
 #pragma unroll
-            for (int b = 0; b < kRowBatch; b++)  // every load of the batch first
+            for (int b = 0; b < B; b++)  // every load of the batch first
                 if (i0 + b * nt < c1) act4_load<XT>(pro, xrow, K, 4 * (i0 + b * nt), norm_w, v[b], aux[b]);
 #pragma unroll
-            for (int b = 0; b < kRowBatch; b++) {
+            for (int b = 0; b < B; b++) {
                 const int i = i0 + b * nt;
                 if (i >= c1) break;
                 act4_apply<XT>(pro, rms, v[b], aux[b]);
@@ -220,19 +219,18 @@ __device__ __forceinline__ int token_exp(float m_all, int bad)
     return (m_all > 0.0f) ? (kQBits - 1) - ilogbf(m_all) : 0;
 }
 
-// Grid (M tokens, row_splits(K) CTAs per token), 256 threads: each token's exponent (and, for
-// kProRmsNorm, its rms).  With a prologue and act_out, the activations are written to act_out
-// [M, K] as well, and the GEMV behind reads them as its x.  With several CTAs per token, each folds its max / Inf-NaN flag into
-// part = [max bits][bad][arrivals], kMaxTokens words each at fixed offsets (zero at rest,
-// whatever M the previous call had), and the last to arrive writes the exponent and re-zeroes
-// its words.  256-thread CTAs fit beside a GEMV CTA on one SM, so the
-// GEMV launched behind this kernel keeps all its CTAs resident.
+// Grid (M tokens, ns = row_splits(K) CTAs per token), 256 threads: CTA (m, sp) scans its share
+// of token m's row and stores one word, part[m * ns + sp] = the bits of its max |a| (a finite
+// float >= 0, so integer order is float order) or -1 if it met an Inf/NaN; the GEMV folds the
+// words into the exponents.  With a prologue, act_out [M, K] receives the activations and the
+// GEMV reads them as its x.  No atomics: nothing sits between the last load and the GEMV's
+// start.  A 256-thread CTA capped at 40 registers fits beside a GEMV CTA (320 threads at <= 168
+// registers) on one SM, so the GEMV launched behind this kernel keeps all its CTAs resident.
 template <typename XT>
-__global__ void __launch_bounds__(kSqThreads) exps_kernel(const XT* __restrict__ x, int K, int* __restrict__ exps,
+__global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restrict__ x, int K,
                                                           const unsigned long long* wait_counts, int wait_n,
                                                           unsigned int wait_seq, int pro, const float* norm_w,
-                                                          float eps, float* __restrict__ rms_out, int* part,
-                                                          XT* __restrict__ act_out)
+                                                          float eps, int* __restrict__ part, XT* __restrict__ act_out)
 {
     pdl_launch_dependents();  // the GEMV may start streaming weights right away
     pdl_wait();               // x is written by the previous kernel
@@ -253,14 +251,13 @@ __global__ void __launch_bounds__(kSqThreads) exps_kernel(const XT* __restrict__
         if (lane == 0) sq[warp] = w;
         __syncthreads();
         rms = rms_from(sq, K, eps);
-        if (sp == 0 && tid == 0) rms_out[m] = rms;
     }
     const int g4 = K >> 2;
     const int c0 = (int)((long long)g4 * sp / ns), c1 = (int)((long long)g4 * (sp + 1) / ns);
     float mx = 0.0f;
     int bad = 0;
-    scan_groups<XT>(pro, xrow, K, norm_w, rms, c0, c1, tid, kSqThreads, mx, bad,
-                    act_out ? act_out + (size_t)m * K : nullptr);
+    scan_groups<XT, 2>(pro, xrow, K, norm_w, rms, c0, c1, tid, kSqThreads, mx, bad,
+                       act_out ? act_out + (size_t)m * K : nullptr);
     if (lane == 0) {
         red[warp] = mx;
         bad_w[warp] = bad;
@@ -273,23 +270,30 @@ __global__ void __launch_bounds__(kSqThreads) exps_kernel(const XT* __restrict__
         m_all = fmaxf(m_all, red[w]);
         b_all |= bad_w[w];
     }
-    if (ns == 1) {
-        exps[m] = token_exp<XT>(m_all, b_all);
-        return;
+    part[(size_t)m * ns + sp] = b_all ? -1 : __float_as_int(m_all);
+}
+
+// The prep kernel's words folded into the tokens' exponents in shared memory, by the epilogue
+// and digitizer warps together (sid 0..255, named barrier 3): warp w takes tokens w, w+8, ...
+template <typename XT>
+__device__ __forceinline__ void fold_prep(const DigParams& p, int sid, int* s_exps)
+{
+    const int sw = sid >> 5, lane = sid & 31;
+    for (int m = sw; m < p.M; m += kSqWarps) {
+        int hi = 0, lo = 0;
+        for (int j = lane; j < p.prep_splits; j += 32) {
+            const int v = p.prep_part[(size_t)m * p.prep_splits + j];
+            hi = max(hi, v);
+            lo = min(lo, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        }
+        if (lane == 0) s_exps[m] = token_exp<XT>(__int_as_float(hi), lo < 0 ? 1 : 0);
     }
-    int* pmax = part;
-    int* pbad = part + kMaxTokens;
-    unsigned int* pcnt = reinterpret_cast<unsigned int*>(part + 2 * kMaxTokens);
-    atomicMax(pmax + m, __float_as_int(m_all));  // m_all >= 0 and finite: int order is float order
-    if (b_all) atomicOr(pbad + m, 1);
-    __threadfence();
-    if (atomicAdd(pcnt + m, 1u) == (unsigned int)ns - 1) {
-        __threadfence();
-        const float mm = __int_as_float(atomicExch(pmax + m, 0));
-        const int bb = atomicExch(pbad + m, 0);
-        atomicExch(pcnt + m, 0u);
-        exps[m] = token_exp<XT>(mm, bb);
-    }
+    asm volatile("bar.sync 3, 256;" ::: "memory");
 }
 
 // The exponents (and rms) of a few tokens, computed inside the GEMV by its epilogue and
@@ -313,7 +317,7 @@ __device__ __forceinline__ void fused_scan(const DigParams& p, int sid, int* s_e
         }
         float mx = 0.0f;
         int bad = 0;
-        scan_groups<XT>(p.pro, xrow, p.K, p.norm_w, rms, 0, p.K >> 2, sid, kSqThreads, mx, bad);
+        scan_groups<XT, 2>(p.pro, xrow, p.K, p.norm_w, rms, 0, p.K >> 2, sid, kSqThreads, mx, bad);
         if (lane == 0) {
             s_red[sw] = mx;
             s_red[kSqWarps + sw] = __int_as_float(bad);
@@ -534,11 +538,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(&g_kernel_error_i8, 2);
             raise_error(abort);
         }
-        if (p.fused_exps || p.po.wait_seq)
+        if (p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed (the epilogue reads them too)
-        // Few tokens: the epilogue and digitizer warps find the per-token exponents themselves.
+        // The per-token exponents into shared memory, by the epilogue and digitizer warps together:
+        // found here for few tokens, else folded from the prep kernel's words.
         if (p.fused_exps) fused_scan<XT>(p, 128 + dtid, s_exps, s_rms, s_red, s_sq);
-        const int* exps = p.fused_exps ? s_exps : p.exps;
+        else fold_prep<XT>(p, 128 + dtid, s_exps);
+        const int* exps = s_exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
         sk::SegIter it(u_begin, u_end, p.kbpt);
@@ -561,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
                     if (k < p.K && e != INT_MIN) {
                         float v[4];
-                        const float rms = p.pro == kProRmsNorm ? (p.fused_exps ? s_rms[m] : p.rms[m]) : 1.0f;
+                        const float rms = p.pro == kProRmsNorm ? s_rms[m] : 1.0f;  // in-kernel prologue only
                         act4<XT>(p.pro, xg + (size_t)m * p.ldx, p.K, k, p.norm_w, rms, v);
 #pragma unroll
                         for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
@@ -583,19 +589,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) raise_error(abort);
     } else {
         // ------------------------------------------------------------ epilogue
-        pdl_wait();  // exps come from the prep kernel
-        // the per-token exponents, once per CTA (they are read for every output)
+        pdl_wait();  // the prep kernel's words are complete
         if (p.amax_keys) {
             if (threadIdx.x - kFirstEpi * 32 < p.M) s_best[threadIdx.x - kFirstEpi * 32] = 0ull;
             asm volatile("bar.sync 1, 128;" ::: "memory");
         }
-        if (p.fused_exps || p.po.wait_seq)
+        if (p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed
+        // the per-token exponents, once per CTA, with the digitizer warps (they are read for every output)
         if (p.fused_exps) fused_scan<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_rms, s_red, s_sq);
-        if (!p.fused_exps) {
-            if (threadIdx.x - kFirstEpi * 32 < p.M) s_exps[threadIdx.x - kFirstEpi * 32] = p.exps[threadIdx.x - kFirstEpi * 32];
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
+        else fold_prep<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps);
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
@@ -887,9 +890,10 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.bias = a.bias;
     p.res = a.res;
     p.out = a.out;
-    // exps scratch: [prep kernel's zero-at-rest words 3 * kMaxTokens][exps M][rms M]
-    int* const exps_base = sc.exps + kPrepWords;
-    p.exps = exps_base;
+    // exps scratch: the prep kernel's words [M][ns]
+    const int ns = row_splits((long long)a.K);
+    p.prep_part = sc.exps;
+    p.prep_splits = ns;
     p.fused_exps = gemv_i8_fused_exps(a) ? 1 : 0;
     p.amax_keys = a.amax_keys;
     p.amax_done = a.amax_done;
@@ -898,7 +902,6 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.norm_w = a.norm_w;
     p.eps = a.eps;
     p.ldx = a.prologue == kProSiluMul ? 2 * (long long)a.K : (long long)a.K;
-    p.rms = reinterpret_cast<const float*>(exps_base + a.M);
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -924,7 +927,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     // reads them as plain x.
     const bool materialize = a.prologue != kProNone && !p.fused_exps;
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
-        sc.exps_count < kPrepWords + 2 * a.M || (materialize && sc.act_bytes < a.M * a.K * sizeof(XT)))
+        sc.exps_count < a.M * (size_t)ns || (materialize && sc.act_bytes < a.M * a.K * sizeof(XT)))
         return cudaErrorMemoryAllocation;
     if (materialize) {
         p.x = sc.act;
@@ -933,10 +936,9 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     }
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
-    e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)row_splits((long long)a.K)), dim3(kSqThreads), 0,
-                  stream, a.pdl, reinterpret_cast<const XT*>(a.x), (int)a.K, exps_base, p.po.wait_counts,
-                  p.po.wait_n, prep_wait_seq, a.prologue, a.norm_w, a.eps, reinterpret_cast<float*>(exps_base + a.M),
-                  sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
+    e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)ns), dim3(kSqThreads), 0, stream, a.pdl,
+                  reinterpret_cast<const XT*>(a.x), (int)a.K, p.po.wait_counts, p.po.wait_n, prep_wait_seq,
+                  a.prologue, a.norm_w, a.eps, sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
     if (e != cudaSuccess) return e;
     return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
 }
@@ -982,7 +984,7 @@ void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, s
     *counters = (size_t)tiles;
     // the prologue's activations, when the prep kernel writes them for the GEMV
     *act_bytes = (a.prologue != kProNone && !gemv_i8_fused_exps(a)) ? a.M * a.K * (a.in_dtype == kF16 ? 2 : 4) : 0;
-    *exps = kPrepWords + 2 * a.M;  // the prep kernel's zero-at-rest words, exponents, the prologue's rms
+    *exps = a.M * (size_t)row_splits((long long)a.K);  // the prep kernel's words
 }
 
 cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch& sc, cudaStream_t stream)
@@ -1030,7 +1032,7 @@ constexpr int kNoAllocMaxTokens = 2;      // 6 digit rows per token: NC = 16
 constexpr int kNoAllocMaxCtas = 160;      // stream-K CTAs (a B200 has 148 SMs)
 constexpr int kNoAllocMaxTiles = 4096;    // 128-row tiles: N <= 524288
 constexpr size_t kNoAllocPartialInts = (size_t)2 * kNoAllocMaxCtas * kTileRows * 16;
-constexpr size_t kNoAllocExps = 256;  // kPrepWords + exponents + rms
+constexpr size_t kNoAllocExps = 256;  // the prep kernel's words: 2 tokens x up to 64 splits
 constexpr size_t kNoAllocBytes = (kNoAllocPartialInts + kNoAllocMaxTiles + kNoAllocExps) * sizeof(int);
 
 }  // namespace
