@@ -46,6 +46,8 @@ typedef struct CUstream_st* b200q8_stream_t;
 #define B200Q8_ERR_NCCL (-4)        /* an NCCL call failed or NCCL is unavailable */
 #define B200Q8_ERR_TIMEOUT (-5)     /* a bounded wait (NCCL init, peer flag) ran out */
 #define B200Q8_ERR_ALLOC (-6)       /* device allocation failed */
+#define B200Q8_ERR_IO (-7)          /* a file could not be opened, mapped or written */
+#define B200Q8_ERR_NOT_FOUND (-8)   /* no tensor of that name in the file */
 
 /* Element types of activations / outputs. */
 #define B200Q8_F32 0
@@ -67,6 +69,13 @@ B200Q8_API uint64_t b200q8_launch_count(void);
  * (replaces include/vvllm/quantize/quantize.h:18, src/quantize/quantize.cc:9-48). */
 B200Q8_API int b200q8_quantize_per_channel(const float* w, size_t N, size_t K, int8_t* q, float* scales,
                                 b200q8_stream_t stream);
+
+/* The same from bfloat16 bits ([N,K] uint16, as a safetensors "BF16" tensor stores them): each
+ * value is widened exactly (bits << 16) as vvllm's loader does (SafeTensorsLoader::bf16_to_f32,
+ * src/safetensors/safetensors.cc:131-137, then quantize_per_channel in
+ * src/model/qwen2/model.cc:27-38), so a checkpoint quantizes on the GPU from its stored bytes. */
+B200Q8_API int b200q8_quantize_per_channel_bf16(const uint16_t* w, size_t N, size_t K, int8_t* q, float* scales,
+                                                b200q8_stream_t stream);
 
 /* out[M,N] = (inp[M,K] . float(weight[N,K])^T) * scales[N] + bias[N]
  * bias may be NULL.  inp is fp32 or fp16 (in_dtype); out is fp32 or fp16
@@ -130,6 +139,53 @@ B200Q8_API int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* in
 B200Q8_API int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dtype,
                                        const int8_t* weight, const float* scales, const float* bias,
                                        size_t M, size_t N, size_t K, int* argmax, b200q8_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Safetensors files on either side of the quantize step (host code).
+ *
+ * vvllm mmaps a safetensors checkpoint (src/safetensors/safetensors.cc:43-83), widens BF16 to
+ * fp32 on the host (:101-117) and quantizes every projection on the host at load
+ * (src/model/qwen2/model.cc:27-38).  b200q8_st_quantize does that quantization once, on the
+ * GPU, and writes a quantized safetensors file; b200q8_st_open reads either kind with the same
+ * layout rules (header parsed once, tensor data returned as pointers into the read-only map).
+ * ------------------------------------------------------------------------ */
+typedef struct b200q8_st b200q8_st;
+
+/* Tensor element types as reported by b200q8_st_info (the file's dtype string otherwise). */
+#define B200Q8_ST_F32 0
+#define B200Q8_ST_F16 1
+#define B200Q8_ST_BF16 2
+#define B200Q8_ST_I8 3
+#define B200Q8_ST_OTHER 4 /* U8, BOOL, I16..U64, F64, F8: carried through unchanged */
+
+/* b200q8_st_quantize flags: also quantize the output head -- "lm_head.weight" (replaced), or
+ * when the model ties it to the embedding, "model.embed_tokens.weight" (kept for the lookup,
+ * quantized copy added). */
+#define B200Q8_ST_LM_HEAD 1u
+
+/* Opens and maps `path`, validates the header (offsets inside the data, sizes matching shapes,
+ * no overlaps, no duplicate names).  Close with b200q8_st_close. */
+B200Q8_API int b200q8_st_open(const char* path, b200q8_st** out);
+B200Q8_API int b200q8_st_close(b200q8_st* f);
+/* Tensors in file-data order: count, then per index its name, type, shape and data (pointers
+ * stay valid until close). */
+B200Q8_API int b200q8_st_count(const b200q8_st* f, size_t* n);
+B200Q8_API int b200q8_st_info(const b200q8_st* f, size_t i, const char** name, int* dtype, size_t* ndim,
+                              const size_t** shape, const void** data, size_t* nbytes);
+/* Index of tensor `name`; B200Q8_ERR_NOT_FOUND if absent. */
+B200Q8_API int b200q8_st_find(const b200q8_st* f, const char* name, size_t* index);
+/* The quantized pair of projection `name` ("<name>.q8" I8 [N, K], "<name>.q8_scales" F32 [N]):
+ * exactly what quantize_per_channel returns for the source weight (QuantizedWeight::data /
+ * scales, include/vvllm/quantize/quantize.h); B200Q8_ERR_NOT_FOUND if the file has none. */
+B200Q8_API int b200q8_st_quantized(const b200q8_st* f, const char* name, size_t* N, size_t* K, const int8_t** q,
+                                   const float** scales);
+/* Writes dst_path: src_path with every 2-D F32/BF16 tensor named "*_proj.weight" (the
+ * projections vvllm quantizes: q/k/v/o, gate/up/down) replaced by its quantized pair, computed
+ * on GPU `device` with the bit-exact quantize kernels; all other tensors are copied byte for
+ * byte and the source metadata is kept (plus a "b200q8" entry).  gate_proj and up_proj stay
+ * separate: quantization is per row, so quantizing their row concatenation (model.cc:66-76)
+ * equals concatenating their quantized rows and scales. */
+B200Q8_API int b200q8_st_quantize(const char* src_path, const char* dst_path, int device, unsigned int flags);
 
 /* Projections with the elementwise op before them fused in.  vvllm runs, per layer,
  *   norm = rms_norm(x) then q/k/v (or gate_up) = linear_q8(norm)

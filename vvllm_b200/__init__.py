@@ -26,6 +26,14 @@ from ._lib import (  # noqa: F401
     linear_q8_sharded,
     linear_q8_sharded_p2p,
     quantize_per_channel,
+    quantize_per_channel_bf16,
+    SafeTensors,
+    st_quantize,
+    ST_BF16,
+    ST_F16,
+    ST_F32,
+    ST_I8,
+    ST_OTHER,
     rms_norm,
     rms_norm_linear_q8,
     shard_range,

@@ -65,6 +65,16 @@ _SIGS = {
     "b200q8_silu_mul_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_rms_norm": ([_vp, _vp, _int, _vp, ctypes.c_float, _sz, _sz, _vp], _int),
     "b200q8_silu_mul": ([_vp, _vp, _int, _sz, _sz, _vp], _int),
+    "b200q8_quantize_per_channel_bf16": ([_vp, _sz, _sz, _vp, _vp, _vp], _int),
+    "b200q8_st_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _int),
+    "b200q8_st_close": ([_vp], _int),
+    "b200q8_st_count": ([_vp, ctypes.POINTER(_sz)], _int),
+    "b200q8_st_info": ([_vp, _sz, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_int), ctypes.POINTER(_sz),
+                        ctypes.POINTER(ctypes.POINTER(_sz)), ctypes.POINTER(_vp), ctypes.POINTER(_sz)], _int),
+    "b200q8_st_find": ([_vp, ctypes.c_char_p, ctypes.POINTER(_sz)], _int),
+    "b200q8_st_quantized": ([_vp, ctypes.c_char_p, ctypes.POINTER(_sz), ctypes.POINTER(_sz), ctypes.POINTER(_vp),
+                             ctypes.POINTER(_vp)], _int),
+    "b200q8_st_quantize": ([ctypes.c_char_p, ctypes.c_char_p, _int, ctypes.c_uint], _int),
 }
 
 # Symbols include/b200q8.h declares (kept in sync by tests/test_abi.py).
@@ -188,6 +198,87 @@ def silu_mul(out, gate_up, stream=None) -> None:
     """out[M,K] = silu(gate_up[:, :K]) * gate_up[:, K:]."""
     M, K2 = gate_up.shape
     _check(lib().b200q8_silu_mul(_addr(out), _addr(gate_up), _dtype_code(gate_up), M, K2 // 2, _stream(stream)))
+
+
+def quantize_per_channel_bf16(w_bits, q, scales, stream=None) -> None:
+    """q[N,K] int8, scales[N] fp32 from bfloat16 bits w_bits[N,K] (int16/uint16 device tensor)."""
+    N, K = w_bits.shape
+    _check(lib().b200q8_quantize_per_channel_bf16(_addr(w_bits), N, K, _addr(q), _addr(scales), _stream(stream)))
+
+
+ST_F32, ST_F16, ST_BF16, ST_I8, ST_OTHER = 0, 1, 2, 3, 4
+ST_LM_HEAD = 1
+_ST_NP = {ST_F32: "float32", ST_F16: "float16", ST_BF16: "uint16", ST_I8: "int8"}
+
+
+class SafeTensors:
+    """A safetensors file opened through b200q8_st_open: tensor data stays in the read-only map
+    (numpy views, valid until close())."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(lib().b200q8_st_open(os.fsencode(path), ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            lib().b200q8_st_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __len__(self) -> int:
+        n = _sz()
+        _check(lib().b200q8_st_count(self._h, ctypes.byref(n)))
+        return n.value
+
+    def info(self, i: int):
+        """(name, dtype code, shape tuple, data address, nbytes) of tensor i (file-data order)."""
+        name, dt, nd, shp, data, nb = ctypes.c_char_p(), _int(), _sz(), ctypes.POINTER(_sz)(), _vp(), _sz()
+        _check(lib().b200q8_st_info(self._h, i, ctypes.byref(name), ctypes.byref(dt), ctypes.byref(nd),
+                                    ctypes.byref(shp), ctypes.byref(data), ctypes.byref(nb)))
+        return name.value.decode(), dt.value, tuple(shp[j] for j in range(nd.value)), data.value or 0, nb.value
+
+    def names(self) -> list[str]:
+        return [self.info(i)[0] for i in range(len(self))]
+
+    def find(self, name: str) -> int:
+        i = _sz()
+        _check(lib().b200q8_st_find(self._h, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    @staticmethod
+    def _view(addr: int, nbytes: int, dtype: str, shape):
+        import numpy as np
+
+        if nbytes == 0:
+            return np.zeros(shape, dtype=dtype)
+        buf = (ctypes.c_char * nbytes).from_address(addr)
+        return np.frombuffer(buf, dtype=dtype).reshape(shape)
+
+    def tensor(self, name: str):
+        """numpy view of a F32 / F16 / BF16 (as uint16 bits) / I8 tensor; raw uint8 bytes otherwise."""
+        _, dt, shape, addr, nb = self.info(self.find(name))
+        if dt in _ST_NP:
+            return self._view(addr, nb, _ST_NP[dt], shape)
+        return self._view(addr, nb, "uint8", (nb,))
+
+    def quantized(self, name: str):
+        """(q int8 [N, K], scales fp32 [N]) of projection `name`, as quantize_per_channel returns them."""
+        N, K, q, sc = _sz(), _sz(), _vp(), _vp()
+        _check(lib().b200q8_st_quantized(self._h, name.encode(), ctypes.byref(N), ctypes.byref(K), ctypes.byref(q),
+                                         ctypes.byref(sc)))
+        return (self._view(q.value or 0, N.value * K.value, "int8", (N.value, K.value)),
+                self._view(sc.value or 0, N.value * 4, "float32", (N.value,)))
+
+
+def st_quantize(src: str, dst: str, device: int = 0, lm_head: bool = False) -> None:
+    """Write dst = src with every projection quantized on GPU `device` (b200q8_st_quantize)."""
+    _check(lib().b200q8_st_quantize(os.fsencode(src), os.fsencode(dst), device, ST_LM_HEAD if lm_head else 0))
 
 
 ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_TC_I8 = 0, 1, 2, 3

@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200q8.so")
 
-SOURCES = ["b200q8_api.cu", "q8_gemv.cu", "q8_quantize.cu", "q8_gemm_tc.cu", "q8_gemv_tc.cu", "gather.cu", "prologue.cu"]
+SOURCES = ["b200q8_api.cu", "q8_gemv.cu", "q8_quantize.cu", "q8_gemm_tc.cu", "q8_gemv_tc.cu", "gather.cu", "prologue.cu", "q8st.cu"]
 HEADERS = ["common.cuh", "kernels.h", "tc_utils.cuh", "sk_common.cuh", "tmap.cuh", "prologue.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -28,10 +28,9 @@ namespace b200q8 {
 static std::atomic<uint64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
-namespace {
-
 thread_local std::string t_last_error;
 
+// Records the message for b200q8_last_error() and returns status.
 int fail(int status, const char* fmt, ...)
 {
     char buf[512];
@@ -47,6 +46,8 @@ int cuda_fail(cudaError_t e, const char* what)
 {
     return fail(B200Q8_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
+
+namespace {
 
 struct DeviceInfo {
     int num_sms = 0;
@@ -330,6 +331,25 @@ int b200q8_quantize_per_channel(const float* w, size_t N, size_t K, int8_t* q, f
     if (st) return st;
     cudaError_t e = launch_q8_quantize(w, N, K, q, scales, d.num_sms, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "q8_quantize launch");
+    return B200Q8_OK;
+}
+
+int b200q8_quantize_per_channel_bf16(const uint16_t* w, size_t N, size_t K, int8_t* q, float* scales,
+                                     b200q8_stream_t stream)
+{
+    if (N == 0) return B200Q8_OK;
+    if (!w || !q || !scales) return fail(B200Q8_ERR_INVALID, "quantize_bf16: null pointer");
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(scales, 0, N * sizeof(float), stream);
+        return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    if (N > (size_t)INT32_MAX || K > ((size_t)1 << 40))
+        return fail(B200Q8_ERR_INVALID, "quantize_bf16: sizes overflow (N=%zu K=%zu)", N, K);
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+    cudaError_t e = launch_q8_quantize_bf16(w, N, K, q, scales, d.num_sms, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "q8_quantize_bf16 launch");
     return B200Q8_OK;
 }
 

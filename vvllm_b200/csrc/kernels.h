@@ -74,6 +74,9 @@ size_t gemv_smem_bytes(int M, int K);
 // Per-row absmax quantization (bit-exact with vvllm::quantize_per_channel).
 cudaError_t launch_q8_quantize(const float* w, size_t N, size_t K, int8_t* q, float* scales,
                                int num_sms, cudaStream_t stream);
+// The same from bf16 bits (widened exactly, bits << 16).
+cudaError_t launch_q8_quantize_bf16(const uint16_t* w, size_t N, size_t K, int8_t* q, float* scales, int num_sms,
+                                    cudaStream_t stream);
 
 // Scratch of the stream-K tensor-core GEMM: fp32 partial accumulators of split
 // tiles and per-tile arrival counters (zero between launches; every launch
@@ -128,6 +131,10 @@ cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, si
 // aligned.  Same arithmetic as the prologue fused into the digit GEMV.
 cudaError_t launch_prologue(int pro, const void* x, void* out, int dtype, const float* norm_w, float eps, size_t M,
                             size_t K, bool pdl, cudaStream_t stream);
+
+// Error reporting of the C ABI: record the message b200q8_last_error() returns, return status.
+int fail(int status, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
 
 // Counts every kernel launch made by this library (for the bench's launch count).
 void note_launch();
