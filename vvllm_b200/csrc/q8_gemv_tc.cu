@@ -70,9 +70,13 @@ constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
 // (saves the prep kernel's launch); longer rows would delay the first digits more than that.
 constexpr int kFusedExpTokens = 4;
 constexpr size_t kFusedExpMaxK = 4096;
+// Longer rows (no prologue) are scanned in-kernel too when the weights are small: there the prep
+// kernel's launch is a large share of the call.  Measured on B200, one fp16 token: Qwen2.5-0.5B
+// down (896 x 4864) 10.9 -> 9.9 us in-kernel; Qwen2-7B down (3584 x 18944) 20.0 -> 20.4 us.
+constexpr size_t kFusedExpMaxKSmall = 20480;
 // With a prologue and few tokens, the in-kernel scan also computes the activations where the
-// digitizers read them, for weights up to this size; above it, and beyond the in-kernel scan's
-// limits, the prep kernel writes them once to scratch and the GEMV reads them as plain x.
+// digitizers read them, for weights up to this size (which also bounds the longer rows above);
+// beyond that the prep kernel writes them once to scratch and the GEMV reads them as plain x.
 // Measured on B200 (one fp16 token): Qwen2.5-0.5B gate_up (9.7 MB) +0.9 us in-kernel vs +1.9 us
 // through the prep kernel; Qwen2-7B gate_up (136 MB) +2.3 us vs +1.2 us (the prep kernel runs
 // while the GEMV's first weight stages load; the in-kernel scan delays the digits).
@@ -184,22 +188,34 @@ __device__ __forceinline__ void scan_groups(int pro, const XT* xrow, int K, cons
         // 8-byte loads: fp16 activations are only required to be 8-byte aligned; the exponent
         // is fixed, only Inf/NaN (exponent field all ones) matter
         const uint2* xr = reinterpret_cast<const uint2*>(xrow);
-        for (int i = c0 + t; i < c1; i += nt) {
-            const uint2 v = xr[i];
-            const uint32_t w[2] = {v.x, v.y};
+        for (int i0 = c0 + t; i0 < c1; i0 += 4 * B * nt) {
+            uint2 v[4 * B];
 #pragma unroll
-            for (int j = 0; j < 2; j++)
-                bad |= (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) ? 1 : 0;
+            for (int b = 0; b < 4 * B; b++)  // every load of the batch first
+                v[b] = (i0 + b * nt < c1) ? xr[i0 + b * nt] : make_uint2(0u, 0u);
+#pragma unroll
+            for (int b = 0; b < 4 * B; b++) {
+                const uint32_t w[2] = {v[b].x, v[b].y};
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    bad |= (((w[j] & 0x7C00u) == 0x7C00u) || ((w[j] & 0x7C000000u) == 0x7C000000u)) ? 1 : 0;
+            }
         }
     } else {
         const float4* xr = reinterpret_cast<const float4*>(xrow);
-        for (int i = c0 + t; i < c1; i += nt) {
-            const float4 v = xr[i];
-            const float a[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
+        for (int i0 = c0 + t; i0 < c1; i0 += 2 * B * nt) {
+            float4 v[2 * B];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                bad |= (a[j] <= FLT_MAX) ? 0 : 1;
-                mx = (a[j] <= FLT_MAX) ? fmaxf(mx, a[j]) : mx;
+            for (int b = 0; b < 2 * B; b++)  // every load of the batch first
+                v[b] = (i0 + b * nt < c1) ? xr[i0 + b * nt] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < 2 * B; b++) {
+                const float a[4] = {fabsf(v[b].x), fabsf(v[b].y), fabsf(v[b].z), fabsf(v[b].w)};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    bad |= (a[j] <= FLT_MAX) ? 0 : 1;
+                    mx = (a[j] <= FLT_MAX) ? fmaxf(mx, a[j]) : mx;
+                }
             }
         }
     }
@@ -961,8 +977,10 @@ int gemv_i8_max_tokens() { return kMaxTokens; }
 
 bool gemv_i8_fused_exps(const LinearArgs& a)
 {
-    return a.M <= (size_t)kFusedExpTokens && a.K <= kFusedExpMaxK &&
-           (a.prologue == kProNone || a.N * a.K <= kPrologueInKernelMaxBytes);
+    if (a.M > (size_t)kFusedExpTokens) return false;
+    const bool small = a.N * a.K <= kPrologueInKernelMaxBytes;
+    if (a.prologue == kProNone) return a.K <= kFusedExpMaxK || (small && a.K <= kFusedExpMaxKSmall);
+    return a.K <= kFusedExpMaxK && small;
 }
 
 bool gemv_i8_supports(const LinearArgs& a)
