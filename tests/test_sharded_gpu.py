@@ -26,9 +26,12 @@ CASES = [
 
 
 CHAIN = [
-    # N1 (= K2), K1, N2: second call's K2 <= 4096 (wait inside its GEMV) and > 4096 (wait kernel)
-    (2048, 896, 640),
-    (6144, 896, 1000),
+    # N1 (= K2), K1, N2, tokens.  The second call waits for the first one's gathered output inside
+    # its GEMV (few tokens, rows up to 4096, or longer rows of small weights) or in its prep kernel
+    # (more than 4 tokens, or long rows of large weights).
+    (2048, 896, 640, 1),
+    (6144, 896, 1000, 1),
+    (3072, 896, 640, 5),
 ]
 
 
@@ -95,9 +98,9 @@ def _worker(rank, world, port, path):
             results[f"full{ci}"] = full.float().cpu().numpy()
             results[f"fullf{ci}"] = fullf.cpu().numpy()
     # Chained gathered calls with deferred waits: y2 = W2 . gather(W1 . x); the second call reads
-    # the first one's gathered output, waiting for it inside its GEMV (K2 <= 4096) or through the
-    # wait kernel ahead of its prep kernel (K2 > 4096); then Comm.wait().
-    for ci, (N1, K1, N2) in enumerate(CHAIN):
+    # the first one's gathered output, waiting for it inside its GEMV or in its prep kernel; then
+    # Comm.wait().
+    for ci, (N1, K1, N2, M) in enumerate(CHAIN):
         data = np.load(os.path.join(path, f"chain{ci}.npz"))
         r1 = v.shard_range(N1, world, rank)
         r2 = v.shard_range(N2, world, rank)
@@ -106,10 +109,10 @@ def _worker(rank, world, port, path):
         q2 = torch.from_numpy(np.ascontiguousarray(data["q2"][r2[0]:r2[0] + r2[1]])).to(dev)
         s2 = torch.from_numpy(data["s2"][r2[0]:r2[0] + r2[1]].copy()).to(dev)
         x = torch.from_numpy(data["x"]).to(dev).half()
-        b1 = -(-N1 * 2 // 256) * 256
-        sym = comm.sym_alloc(b1 + N2 * 2)
-        y1 = sym[:N1 * 2].view(torch.float16).view(1, N1)
-        y2 = sym[b1:b1 + N2 * 2].view(torch.float16).view(1, N2)
+        b1 = -(-M * N1 * 2 // 256) * 256
+        sym = comm.sym_alloc(b1 + M * N2 * 2)
+        y1 = sym[:M * N1 * 2].view(torch.float16).view(M, N1)
+        y2 = sym[b1:b1 + M * N2 * 2].view(torch.float16).view(M, N2)
         for _ in range(3):
             v.linear_q8_sharded_p2p(comm, y1, x, q1, s1, None, N1, defer_wait=True)
             v.linear_q8_sharded_p2p(comm, y2, y1, q2, s2, None, N2, defer_wait=True)
@@ -117,8 +120,8 @@ def _worker(rank, world, port, path):
         torch.cuda.synchronize()
         results[f"chain{ci}"] = y2.float().cpu().numpy()
         if rank == 0:
-            f1 = torch.empty((1, N1), dtype=torch.float16, device=dev)
-            f2 = torch.empty((1, N2), dtype=torch.float16, device=dev)
+            f1 = torch.empty((M, N1), dtype=torch.float16, device=dev)
+            f2 = torch.empty((M, N2), dtype=torch.float16, device=dev)
             v.linear_q8(f1, x, torch.from_numpy(data["q1"]).to(dev), torch.from_numpy(data["s1"]).to(dev))
             v.linear_q8(f2, f1, torch.from_numpy(data["q2"]).to(dev), torch.from_numpy(data["s2"]).to(dev))
             torch.cuda.synchronize()
@@ -144,10 +147,10 @@ def test_sharded_two_gpus(tmp_path, oracle):
         q, s = oracle.quantize_per_channel(make_weight(N, K, 900 + ci))
         x = make_x(M, K, 910 + ci).astype(np.float16).astype(np.float32)
         np.savez(tmp_path / f"case{ci}.npz", q=q, s=s, x=x)
-    for ci, (N1, K1, N2) in enumerate(CHAIN):
+    for ci, (N1, K1, N2, M) in enumerate(CHAIN):
         q1, s1 = oracle.quantize_per_channel(make_weight(N1, K1, 950 + ci))
         q2, s2 = oracle.quantize_per_channel(make_weight(N2, N1, 960 + ci))
-        x = make_x(1, K1, 970 + ci).astype(np.float16).astype(np.float32)
+        x = make_x(M, K1, 970 + ci).astype(np.float16).astype(np.float32)
         np.savez(tmp_path / f"chain{ci}.npz", q1=q1, s1=s1, q2=q2, s2=s2, x=x)
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
