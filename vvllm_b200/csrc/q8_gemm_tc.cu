@@ -704,7 +704,11 @@ int pick_bn(size_t M, size_t N, int num_sms)
     if (M <= 32) return 32;
     if (M <= 64) return 64;
     if (M <= 128) return 128;
-    const long long tiles256 = (long long)((N + kTileRows - 1) / kTileRows) * (long long)((M + 255) / 256);
+    const long long tiles_n = (long long)((N + kTileRows - 1) / kTileRows);
+    // Small problems whose 32-token tiles all fit on the SMs run fastest as many narrow whole
+    // tiles (measured on B200 at M = 512: 896x896 16.0 -> 14.2 us, 4864x896 32.7 -> 28.2 us).
+    if (tiles_n * (long long)((M + 31) / 32) <= num_sms) return 32;
+    const long long tiles256 = tiles_n * (long long)((M + 255) / 256);
     return 4 * tiles256 >= num_sms ? 256 : 128;
 }
 int pick_bk(int BN) { return BN <= 32 ? 256 : BN <= 128 ? 128 : 64; }

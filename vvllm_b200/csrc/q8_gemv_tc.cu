@@ -156,6 +156,20 @@ __device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsign
     return true;
 }
 
+// Bounded wait until a split tile's arrival counter reaches `target` (read with gpu-scope
+// acquire); false after timeout_ns or once the CTA aborts.
+__device__ bool wait_tile_pieces(const int* ctr, int target, volatile int* abort, uint64_t timeout_ns)
+{
+    const uint64_t t0 = tc::globaltimer_ns();
+    for (;;) {
+        int seen;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
+        if (seen >= target) return true;
+        if (*abort || tc::globaltimer_ns() - t0 > timeout_ns) return false;
+        __nanosleep(32);
+    }
+}
+
 // ----------------------------------------------------------------------------- prep
 // max |a| over the 4-element groups [c0, c1) of one token's row taken by thread t of nt, and
 // whether any a is Inf/NaN; a is x or, with a prologue, the activations it makes from x, which
@@ -415,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sD + S * C::kDBytes);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]
+    // tmem_holder[2..3]: spare
     int* s_exps = reinterpret_cast<int*>(tmem_holder + 4);                          // [kMaxTokens]
     float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [16] exponent reduction
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(                 // [kMaxTokens] argmax keys
@@ -623,8 +637,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         int seg = 0, t, k0, k1;
         sk::SegIter it(u_begin, u_end, p.kbpt);
         bool ok = true;
-        OT* out = reinterpret_cast<OT*>(p.out);
-        const OT* res = reinterpret_cast<const OT*>(p.res);
         const int ncols = kDigits * p.M;
         while (it.next(t, k0, k1)) {
             const int ab = seg & 1, use = seg >> 1;
@@ -642,18 +654,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const long long tb = (long long)t * p.kbpt;
             const int j0 = whole ? cta : sk::cta_of_unit(tb, p.units, G);
             const int j1 = whole ? cta : sk::cta_of_unit(tb + p.kbpt - 1, p.units, G);
-            volatile int* lf = last_flag + (seg == 0 ? 0 : 1);
             bool last = whole;
-            if (!whole) {
-                // A piece that finds every other piece already in is the last one: it reduces
-                // with its own digit sums taken straight from TMEM, skipping its own round trip.
-                if (etid == 0) {
-                    int seen;
-                    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(p.counters + t) : "memory");
-                    *lf = (seen == j1 - j0) ? 1 : 0;
-                }
+            if (!whole && cta == j0) {
+                // The piece holding the tile's first k-blocks reduces.  CTA j0 reaches them at the
+                // end of its range, after the other pieces' CTAs have done theirs at the start of
+                // theirs, so it rarely waits; it adds the other pieces' stored sums to its own taken
+                // straight from TMEM.  Bounded wait: the pieces come from co-resident CTAs of
+                // higher index whose waits, if any, are in later segments.
+                if (etid == 0 && !wait_tile_pieces(p.counters + t, j1 - j0, abort, kWaitTimeoutNs))
+                    raise_error(abort);
                 asm volatile("bar.sync 1, 128;" ::: "memory");
-                last = *lf != 0;
+                last = true;
             }
             const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
             int* wrow = p.ws + ((size_t)slot * kTileRows + r) * NC;
@@ -752,17 +763,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     break;
                 }
-                // this piece's sums are out: count it in; the last one to arrive reduces
+                // this piece's sums are out: count it in for the reducing piece
                 __threadfence();
                 asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (etid == 0) {
-                    const int prev = atomicAdd(p.counters + t, 1);
-                    *lf = (prev == j1 - j0) ? 1 : 0;
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (!*lf) break;
-                last = true;
-                __threadfence();  // acquire: the other pieces' sums
+                if (etid == 0) atomicAdd(p.counters + t, 1);
+                break;
             }
             tc::tc_fence_before();
             __syncwarp();
