@@ -669,8 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int slot = (seg == 0) ? 2 * cta : 2 * cta + 1;
             int* wrow = p.ws + ((size_t)slot * kTileRows + r) * NC;
             // Each token's six digit sums sit in consecutive TMEM columns; take kGT tokens (kGC
-            // columns, 16-column loads) at a time.  A non-last piece stores them to its
-            // workspace slot; the last piece adds every other piece's sums (all loads in flight)
+            // columns, 16-column loads) at a time.  A non-reducing piece stores them to its
+            // workspace slot; the reducing piece adds every other piece's sums (all loads in flight)
             // and writes the outputs.
             constexpr int kGT = NC >= 48 ? 8 : NC / kDigits;     // tokens per group
             constexpr int kGC = (kGT * kDigits + 15) / 16 * 16;  // TMEM columns per group
@@ -836,7 +836,7 @@ bool make_i8_map(CUtensorMap* m, const void* base, size_t K, size_t rows, int bo
 
 // Grid size.  All SMs share HBM, so the stream needs enough of them (one SM pulls ~75 GB/s with
 // its 3-stage ring), but every extra CTA on a tile is one more stream-K piece whose partial the
-// last piece must fetch (four pieces per round trip of ~1 us).  Few-tile long-K shapes (a 7B
+// reducing piece must fetch (four pieces per round trip of ~1 us).  Few-tile long-K shapes (a 7B
 // down projection sharded 8 ways: 4 tiles of 37 K-stages) would otherwise split each tile into
 // dozens of pieces; this takes the grid (all SMs, or a whole number of CTAs per tile) with the
 // lowest estimated stream + fixup time, preferring more CTAs on ties.
