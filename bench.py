@@ -283,6 +283,82 @@ def prefill_tflops(v, dev, stream, warmup: int, iters: int, tc_peak: float):
             "timing": "median CUDA-graph replay (device time), L2 flushed before each replay"}
 
 
+def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
+    """BASELINE configs 2 and 3 as whole decode stacks at M = 1, each step one CUDA-graph replay
+    of every projection of every layer in order (the library's ctypes host call costs more than
+    the small projections take on the device):
+      SmolLM-135M-shaped, fp32 activations: 30 x {q 576, k/v 576->192, o 576 (+residual),
+        gate|up 576->3072 (fused as the reference model fuses them), down 1536->576 (+residual)},
+        lm_head 576->49152; 136.7 MB of weights, two copies alternated so a cycle exceeds 2x L2;
+      Qwen2.5-0.5B-shaped, fp16 activations: 24 x {q 896 (+bias), k/v 896->128 (+bias),
+        o 896 (+residual), gate|up 896->9728, down 4864->896 (+residual)}, tied lm_head
+        896->151936; 494 MB of weights (> 2x L2).
+    value = algorithmic bytes of the step (weights, scales, biases, activations, outputs and the
+    residual reads) / median device time of one replay."""
+    import torch
+
+    torch.manual_seed(2)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def stack(layers, hidden, kv, inter, vocab, bias_qkv, in16, copies):
+        adt = torch.float16 if in16 else torch.float32
+        a = 2 if in16 else 4
+        shapes = []  # (N, K, has_bias, residual)
+        for _ in range(layers):
+            shapes += [(hidden, hidden, bias_qkv, False), (kv, hidden, bias_qkv, False), (kv, hidden, bias_qkv, False),
+                       (hidden, hidden, False, True), (2 * inter, hidden, False, False), (hidden, inter, False, True)]
+        shapes.append((vocab, hidden, False, False))
+        sets = []
+        for _ in range(copies):
+            calls = []
+            for N, K, hb, res in shapes:
+                q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+                sc = torch.rand(N, device=dev) * 1e-3
+                b = torch.randn(N, device=dev) * 0.1 if hb else None
+                x = torch.randn(1, K, device=dev).to(adt)
+                out = torch.randn(1, N, device=dev).to(adt)
+                calls.append((q, sc, b, x, out, res))
+            sets.append(calls)
+        nbytes = sum(algo_bytes(N, K, 1, a, a) + (4 * N if hb else 0) + (a * N if res else 0)
+                     for N, K, hb, res in shapes)
+
+        def run(calls):
+            for q, sc, b, x, out, res in calls:
+                if res:
+                    v.linear_q8_add(out, x, q, sc, b, out, stream=stream)
+                else:
+                    v.linear_q8(out, x, q, sc, b, stream=stream)
+
+        graphs = []
+        for calls in sets:
+            for _ in range(warmup):
+                run(calls)
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run(calls)
+            graphs.append(g)
+        ms = []
+        with torch.cuda.stream(stream):
+            for i in range(iters * copies):
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                graphs[i % copies].replay()
+                a1.record(stream)
+                a1.synchronize()
+                ms.append(a0.elapsed_time(a1))
+        del graphs
+        t = statistics.median(ms)
+        gbs = nbytes / (t * 1e-3) / 1e9
+        return {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "us": round(t * 1e3, 2),
+                "calls": len(shapes), "bytes": nbytes, "weight_copies": copies}
+
+    return {"smollm135m_fp32": stack(30, 576, 192, 1536, 49152, False, False, 2),
+            "qwen05b_fp16": stack(24, 896, 128, 4864, 151936, True, True, 1),
+            "timing": "median CUDA-graph replay of one whole step (device time), weights cycled beyond L2"}
+
+
 def profile_case(args):
     """Small single-projection run for ncu: warmup + 1 launches of one linear_q8 on one GPU.
     Weights are random int8 made with one torch launch (values do not change the memory traffic)."""
@@ -531,9 +607,10 @@ def main():
     e2e_value = total_bytes / (e_ms / args.steps * 1e-3) / 1e9
 
     # ---- prefill GEMM TFLOP/s (M = 512, fp16 in/out), rank 0 at N = 1 ------
-    prefill = None
+    prefill = stacks = None
     if world == 1:
         prefill = prefill_tflops(v, dev, stream, args.warmup, max(5, args.steps // 10), tc_peak)
+        stacks = decode_stacks(v, dev, args.warmup, max(10, args.steps // 10), hbm_peak)
 
     # ---- CPU baseline: the reference's linear_q8 on the host cores (rank 0, N = 1) ------------
     cpu_baseline = None
@@ -581,6 +658,8 @@ def main():
             line["gemv_then_nccl_allgather"] = nccl_leg
         if prefill is not None:
             line["prefill"] = prefill
+        if stacks is not None:
+            line["decode_stacks"] = stacks
         if cpu_baseline is not None:
             line["cpu_baseline"] = cpu_baseline
         print(json.dumps(line), flush=True)

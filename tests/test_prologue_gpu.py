@@ -150,7 +150,7 @@ def test_silu_mul_no_residual(cuda, oracle):
 @pytest.mark.parametrize("in16", [False, True])
 def test_prologue_edge_rows(cuda, oracle, in16):
     """Zero row (rms = sqrt(eps)), a NaN row and an overflowing row give the same results fused and
-    unfused; a NaN / Inf activation row yields NaN outputs for its token."""
+    unfused; a NaN / Inf activation row yields non-finite outputs for its token."""
     import torch
 
     import vvllm_b200 as v
@@ -194,7 +194,9 @@ def test_prologue_edge_rows(cuda, oracle, in16):
     assert _same(fused2, plain2)
     y2 = fused2.cpu().numpy()
     assert np.isfinite(y2[0]).all()
-    assert np.isnan(y2[1]).all() == in16
+    # an Inf activation makes every output of its token non-finite: NaN on the digit GEMV,
+    # +-Inf (NaN where it meets a zero weight) on the SIMT GEMV, which takes this small shape
+    assert (~np.isfinite(y2[1])).all() == in16
 
 
 def test_prologue_rejects_bad_shapes(cuda):

@@ -177,6 +177,9 @@ int reset_scratch_counters(int dev)
     return B200Q8_OK;
 }
 
+// Weights up to this size with few tokens go to the SIMT GEMV under ALGO_AUTO.
+constexpr size_t kSimtMaxWeightBytes = (size_t)32 << 20;
+
 // pro / norm_w / eps: an elementwise prologue (prologue.cuh) that turns inp into the activations
 // -- fused into the int8 digit GEMV, or run first into scratch when the GEMM takes the shape.
 int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,
@@ -221,10 +224,15 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     a.out_dtype = out_dtype;
     a.pdl = true;
     cudaError_t e;
-    // Kernel choice (AUTO): up to 16 tokens -> int8 tensor-core GEMV with exact activation digits;
-    // more tokens with fp16 activations -> fp16 tensor-core GEMM (weights dequantized into TMEM);
-    // more tokens with fp32 activations -> the digit kernel in groups of up to 42 tokens.
-    // Shapes the tensor-core kernels cannot take (K % 16 != 0, misaligned) use the SIMT GEMV.
+    // Kernel choice (AUTO): up to 4 tokens on at most 32 MiB of weights -> the SIMT streaming GEMV
+    // (the tensor-core kernels' fixed costs -- barrier and TMEM set-up, pipeline fill, stream-K
+    // fixup, ~6 us -- exceed a few-MB projection's whole streaming time: measured on B200, one
+    // token, 896x896 2.5 vs 6.0 us, 896x4864 4.6 vs 9.6 us, 49152x576 12.2 vs 12.5 us, and a
+    // Qwen2.5-0.5B decode step 555 vs 1070 us); up to 16 tokens -> int8 tensor-core GEMV with
+    // exact activation digits; more tokens with fp16 activations -> fp16 tensor-core GEMM
+    // (weights dequantized into TMEM); more tokens with fp32 activations -> the digit kernel in
+    // groups of up to 42 tokens.  Shapes the tensor-core kernels cannot take (K % 16 != 0,
+    // misaligned) use the SIMT GEMV.
     const bool tc_ok = gemm_tc_supports(a);
     LinearArgs a1 = a;
     a1.M = M < (size_t)gemv_i8_max_tokens() ? M : (size_t)gemv_i8_max_tokens();
@@ -237,9 +245,11 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
         return fail(B200Q8_ERR_UNSUPPORTED,
                     "linear_q8: int8 tensor-core path needs K %% 16 == 0, K <= 131072 and a 16-byte aligned "
                     "weight pointer (K=%zu)", K);
+    const bool small = M <= (size_t)gemv_max_tokens() && N * K <= kSimtMaxWeightBytes;
     const bool use_i8 = algo == B200Q8_ALGO_TC_I8 ||
-                        (algo == B200Q8_ALGO_AUTO && i8_ok && (M <= 16 || !tc_ok));
-    const bool use_tc = !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok));
+                        (algo == B200Q8_ALGO_AUTO && i8_ok && !small && (M <= 16 || !tc_ok));
+    const bool use_tc =
+        !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok && !small));
     if (pro != kProNone && !use_i8) {
         // The GEMM (or SIMT) kernel reads plain activations: write them once into scratch.
         ScratchNeed need;

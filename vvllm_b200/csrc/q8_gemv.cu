@@ -131,7 +131,16 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
     const int rows_per_cta = RW * R;
     const int num_groups = (p.N + rows_per_cta - 1) / rows_per_cta;
 
-    // x is produced by the previous kernel in the stream.
+    // The weights do not depend on the previous kernel in the stream, x does: pull this CTA's
+    // first row group (one contiguous range of rows_per_cta rows, 16-byte aligned on this path)
+    // into L2 while that kernel finishes, then wait.
+    if (threadIdx.x == 0 && (int)blockIdx.x < num_groups) {
+        const int r0 = (int)blockIdx.x * rows_per_cta;
+        const int nr = min(rows_per_cta, p.N - r0);
+        const unsigned bytes = (unsigned)((long long)nr * p.K);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.w + (long long)r0 * p.K), "r"(bytes)
+                     : "memory");
+    }
     pdl_wait();
     stage_x<XT>(xs4, reinterpret_cast<const XT*>(p.x), p.ldx, p.M, p.K);
     __syncthreads();
