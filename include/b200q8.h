@@ -195,9 +195,10 @@ B200Q8_API int b200q8_st_quantize(const char* src_path, const char* dst_path, in
  *   h = silu_mul(gate_up[:, :K], gate_up[:, K:]) then x = linear_q8_add(h, x)
  *     (transformer.h:171-188; backend_naive.cc:293-300).
  * These compute the same results with the elementwise op done where the projection reads its
- * activations: for the int8 decode GEMV (up to 16 fp16 / any number of fp32 tokens) it runs
- * inside that kernel, so the normalised / gated activations never go to memory and the extra
- * launch disappears; for the fp16 prefill GEMM it runs first as its own kernel into scratch.
+ * activations: for few tokens on small weights the streaming GEMV applies it while it stages
+ * x (one launch, nothing written); for the int8 tensor-core GEMV its per-token prep kernel
+ * applies it and writes the activations once; for the fp16 prefill GEMM it runs first as its
+ * own kernel into scratch.
  * Arithmetic: rms = sqrt(sum_k x^2 / K + eps) (sum taken in double, one fixed order), then
  * x / rms * w; silu_mul = (g / (1 + exp(-g))) * u.  With fp16 activations the norm weight is
  * rounded to fp16 and the result to fp16, as vvllm's fp16 backend does

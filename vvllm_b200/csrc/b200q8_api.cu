@@ -250,8 +250,18 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
                         (algo == B200Q8_ALGO_AUTO && i8_ok && !small && (M <= 16 || !tc_ok));
     const bool use_tc =
         !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok && !small));
-    if (pro != kProNone && !use_i8) {
-        // The GEMM (or SIMT) kernel reads plain activations: write them once into scratch.
+    // The SIMT streaming kernel applies a prologue while it stages x (one launch); so does the
+    // digit GEMV.  For the GEMM, or SIMT shapes only its generic kernel takes, write the
+    // activations once into scratch first.
+    bool simt_pro = false;
+    if (pro != kProNone && !use_i8 && !use_tc) {
+        LinearArgs s1 = a;
+        s1.M = M < (size_t)gemv_max_tokens() ? M : (size_t)gemv_max_tokens();
+        s1.prologue = pro;
+        s1.norm_w = norm_w;
+        simt_pro = gemv_stream_supports(s1, d.max_smem);
+    }
+    if (pro != kProNone && !use_i8 && !simt_pro) {
         ScratchNeed need;
         need.act = M * K * ib;
         TcScratch scratch;
@@ -300,10 +310,11 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     // M beyond the GEMV's token count and not taken by the tensor-core GEMM:
     // stream the weights once per group of up to 4 tokens.
     const int mt = gemv_max_tokens();
+    const size_t xstride = pro == kProSiluMul ? 2 * K : K;  // input row length (prologue not materialized)
     for (size_t m0 = 0; m0 < M; m0 += (size_t)mt) {
         LinearArgs b = a;
         b.M = (M - m0 < (size_t)mt) ? (M - m0) : (size_t)mt;
-        b.x = (const char*)inp + m0 * K * ib;
+        b.x = (const char*)inp + m0 * xstride * ib;
         b.out = (char*)out + m0 * N * ob;
         b.res = residual ? (const char*)residual + m0 * N * ob : nullptr;
         e = launch_q8_gemv(b, d.num_sms, d.max_smem, stream);

@@ -68,6 +68,9 @@ cudaError_t read_kernel_error_p2p(int* code, bool clear);
 // Streaming SIMT GEMV, M <= gemv_max_tokens().  Also takes any M/K through a
 // generic (slow, correct) kernel when the fast one cannot (alignment, K % 16).
 cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cudaStream_t stream);
+// The streaming SIMT kernel takes the shape (aligned, K % 16 == 0, M <= 4, x fits in shared
+// memory); only then may a.prologue be set (it is applied while x is staged).
+bool gemv_stream_supports(const LinearArgs& a, size_t max_smem);
 int gemv_max_tokens();
 size_t gemv_smem_bytes(int M, int K);
 

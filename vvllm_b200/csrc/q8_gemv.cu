@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "prologue.cuh"
 
 namespace b200q8 {
 
@@ -48,7 +49,11 @@ struct GemvParams {
     long long ldx, ldo;
     int N, K, M;         // M <= MT
     int KW;              // K slices per CTA (1, 2, 4, 8)
+    int pro;             // prologue applied while x is staged (prologue.cuh); x rows are ldx apart
+    const float* norm_w;
+    float eps;
 };
+static_assert(kThreads == kSqThreads, "the prologue's fixed-order sum is taken by one 256-thread CTA");
 
 template <typename XT>
 __device__ __forceinline__ void stage_x(float4* xs4, const XT* x, long long ldx, int M, int K);
@@ -87,6 +92,45 @@ __device__ __forceinline__ void stage_x<__half>(float4* xs4, const __half* x, lo
             const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
             xs4[(t * 4 + 2 * h) * C + c] = make_float4(a.x, a.y, b.x, b.y);
             xs4[(t * 4 + 2 * h + 1) * C + c] = make_float4(d.x, d.y, e.x, e.y);
+        }
+    }
+}
+
+// The prologue's activations staged like stage_x<float> stages x: the same act4 values the fused
+// digit GEMV and the standalone prologue kernel compute (the token's rms from the shared
+// fixed-order sum of this 256-thread CTA), so the projection equals the standalone op followed
+// by the plain GEMV bit for bit.
+// (Out of line: it runs once per CTA and must not take registers from the streaming loop.)
+template <typename XT>
+__device__ __noinline__ void stage_x_pro(float4* xs4, const XT* x, long long ldx, int M, int K, int pro,
+                                         const float* norm_w, float eps)
+{
+    __shared__ double sq[kSqWarps];
+    const int C = K >> 4;
+    const int g4 = K >> 2;
+    for (int t = 0; t < M; t++) {
+        const XT* xrow = x + (long long)t * ldx;
+        float rms = 1.0f;
+        if (pro == kProRmsNorm) {
+            const double w = sumsq_warp<XT>(xrow, K, threadIdx.x);
+            if ((threadIdx.x & 31) == 0) sq[threadIdx.x >> 5] = w;
+            __syncthreads();
+            rms = rms_from(sq, K, eps);
+            __syncthreads();  // sq is reused by the next token
+        }
+        for (int i0 = threadIdx.x; i0 < g4; i0 += 2 * kThreads) {
+            float v[2][4], aux[2][4];
+#pragma unroll
+            for (int b = 0; b < 2; b++)  // both groups' loads first
+                if (i0 + b * kThreads < g4) act4_load<XT>(pro, xrow, K, 4 * (i0 + b * kThreads), norm_w, v[b], aux[b]);
+#pragma unroll
+            for (int b = 0; b < 2; b++) {
+                const int i = i0 + b * kThreads;
+                if (i < g4) {
+                    act4_apply<XT>(pro, rms, v[b], aux[b]);
+                    xs4[(t * 4 + (i & 3)) * C + (i >> 2)] = make_float4(v[b][0], v[b][1], v[b][2], v[b][3]);
+                }
+            }
         }
     }
 }
@@ -142,7 +186,10 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
                      : "memory");
     }
     pdl_wait();
-    stage_x<XT>(xs4, reinterpret_cast<const XT*>(p.x), p.ldx, p.M, p.K);
+    if (p.pro != kProNone)
+        stage_x_pro<XT>(xs4, reinterpret_cast<const XT*>(p.x), p.ldx, p.M, p.K, p.pro, p.norm_w, p.eps);
+    else
+        stage_x<XT>(xs4, reinterpret_cast<const XT*>(p.x), p.ldx, p.M, p.K);
     __syncthreads();
     pdl_launch_dependents();
 
@@ -364,6 +411,15 @@ int gemv_max_tokens() { return 4; }
 
 size_t gemv_smem_bytes(int M, int K) { return (size_t)M * K * sizeof(float) + 2 * kWarps * 8 * sizeof(float); }
 
+bool gemv_stream_supports(const LinearArgs& a, size_t max_smem)
+{
+    const size_t xbytes = a.in_dtype == kF16 ? 2 : 4;
+    const bool aligned = (a.K % 16 == 0) && ((uintptr_t)a.w % 16 == 0) && ((uintptr_t)a.x % 16 == 0) &&
+                         ((a.K * xbytes) % 16 == 0) && (a.prologue != kProRmsNorm || (uintptr_t)a.norm_w % 16 == 0);
+    const int mt = a.M <= 1 ? 1 : (a.M == 2 ? 2 : 4);
+    return aligned && a.M <= 4 && a.K <= (size_t)INT32_MAX && gemv_smem_bytes(mt, (int)a.K) <= max_smem;
+}
+
 cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cudaStream_t stream)
 {
     GemvParams p{};
@@ -373,25 +429,24 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
     p.bias = a.bias;
     p.res = a.res;
     p.out = a.out;
-    p.ldx = a.K;
+    p.ldx = a.prologue == kProSiluMul ? 2 * (long long)a.K : (long long)a.K;
     p.ldo = a.N;
     p.N = (int)a.N;
     p.K = (int)a.K;
     p.M = (int)a.M;
     p.KW = 1;
+    p.pro = a.prologue;
+    p.norm_w = a.norm_w;
+    p.eps = a.eps;
     const bool x16 = (a.in_dtype == kF16);
     const bool o16 = (a.out_dtype == kF16);
-    const size_t xbytes = x16 ? 2 : 4;
-    const bool aligned = (a.K % 16 == 0) && ((uintptr_t)a.w % 16 == 0) && ((uintptr_t)a.x % 16 == 0) &&
-                         ((a.K * xbytes) % 16 == 0);
-    const int mt = a.M <= 1 ? 1 : (a.M == 2 ? 2 : 4);
-    const bool fits = gemv_smem_bytes(mt, (int)a.K) <= max_smem && a.M <= 4;
-    if (aligned && fits) {
+    if (gemv_stream_supports(a, max_smem)) {
         if (x16) return o16 ? dispatch_typed<__half, __half>(p, num_sms, stream, a.pdl)
                             : dispatch_typed<__half, float>(p, num_sms, stream, a.pdl);
         return o16 ? dispatch_typed<float, __half>(p, num_sms, stream, a.pdl)
                    : dispatch_typed<float, float>(p, num_sms, stream, a.pdl);
     }
+    if (a.prologue != kProNone) return cudaErrorNotSupported;  // the generic kernel reads plain x
     if (x16) return o16 ? dispatch_generic<__half, __half>(p, stream, a.pdl)
                         : dispatch_generic<__half, float>(p, stream, a.pdl);
     return o16 ? dispatch_generic<float, __half>(p, stream, a.pdl)

@@ -70,17 +70,12 @@ constexpr int kMaxTokens = 42;  // 6 * 42 = 252 <= 256 digit rows
 // (saves the prep kernel's launch); longer rows would delay the first digits more than that.
 constexpr int kFusedExpTokens = 4;
 constexpr size_t kFusedExpMaxK = 4096;
-// Longer rows (no prologue) are scanned in-kernel too when the weights are small: there the prep
-// kernel's launch is a large share of the call.  Measured on B200, one fp16 token: Qwen2.5-0.5B
+// Longer rows are scanned in-kernel too when the weights are small (the next constant): there
+// the prep kernel's launch is a large share of the call.  Measured on B200, one fp16 token: Qwen2.5-0.5B
 // down (896 x 4864) 10.9 -> 9.9 us in-kernel; Qwen2-7B down (3584 x 18944) 20.0 -> 20.4 us.
 constexpr size_t kFusedExpMaxKSmall = 20480;
-// With a prologue and few tokens, the in-kernel scan also computes the activations where the
-// digitizers read them, for weights up to this size (which also bounds the longer rows above);
-// beyond that the prep kernel writes them once to scratch and the GEMV reads them as plain x.
-// Measured on B200 (one fp16 token): Qwen2.5-0.5B gate_up (9.7 MB) +0.9 us in-kernel vs +1.9 us
-// through the prep kernel; Qwen2-7B gate_up (136 MB) +2.3 us vs +1.2 us (the prep kernel runs
-// while the GEMV's first weight stages load; the in-kernel scan delays the digits).
-constexpr size_t kPrologueInKernelMaxBytes = (size_t)32 << 20;
+// ... for weights up to this size.
+constexpr size_t kInKernelScanMaxBytes = (size_t)32 << 20;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 constexpr uint64_t kPeerTimeoutNs = 2000000000ull;  // a peer's flag of the previous gathered call
 
@@ -104,11 +99,6 @@ struct DigParams {
     unsigned long long* amax_keys;  // [M]
     unsigned int* amax_done;        // CTAs finished, zero between launches
     int* amax_out;                  // [M] result
-    // Prologue (prologue.cuh) applied where the digitizers read x; x rows are ldx apart.
-    int pro;
-    const float* norm_w;
-    float eps;
-    long long ldx;
 };
 
 template <int NC, int BK, int S>
@@ -123,8 +113,7 @@ struct DigCfg {
                                      : kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kNumBars = 3 * S + 4 + 1;  // full, dfull, empty per stage; acc x4; drain
     static constexpr int kSmemBytes =
-        1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 64 + 8 * kMaxTokens + 8 + 64 +
-        4 * kMaxTokens;
+        1024 + S * (kWBytes + kDBytes) + kNumBars * 8 + 16 + 4 * kMaxTokens + 64 + 8 * kMaxTokens + 8;
     static_assert(NC % 16 == 0 && NC >= 16 && NC <= 256, "kind::i8 N for M=128");
     static_assert(BK % 128 == 0, "whole 128-byte boxes");
     static_assert(kColsNeeded <= 512, "TMEM overflow");
@@ -326,28 +315,18 @@ __device__ __forceinline__ void fold_prep(const DigParams& p, int sid, int* s_ex
     asm volatile("bar.sync 3, 256;" ::: "memory");
 }
 
-// The exponents (and rms) of a few tokens, computed inside the GEMV by its epilogue and
-// digitizer warps together (sid 0..255, named barrier 3), with the prep kernel's rules and the
-// same fixed-order sum of squares.
+// The exponents of a few tokens, computed inside the GEMV by its epilogue and digitizer warps
+// together (sid 0..255, named barrier 3), with the prep kernel's rules.
 template <typename XT>
-__device__ __forceinline__ void fused_scan(const DigParams& p, int sid, int* s_exps, float* s_rms, float* s_red,
-                                           double* s_sq)
+__device__ __forceinline__ void fused_scan(const DigParams& p, int sid, int* s_exps, float* s_red)
 {
     const int sw = sid >> 5, lane = sid & 31;
 #pragma unroll 1
     for (int m = 0; m < p.M; m++) {
-        const XT* xrow = reinterpret_cast<const XT*>(p.x) + (size_t)m * p.ldx;
-        float rms = 1.0f;
-        if (p.pro == kProRmsNorm) {
-            const double w = sumsq_warp<XT>(xrow, p.K, sid);
-            if (lane == 0) s_sq[sw] = w;
-            asm volatile("bar.sync 3, 256;" ::: "memory");
-            rms = rms_from(s_sq, p.K, p.eps);
-            if (sid == 0) s_rms[m] = rms;
-        }
+        const XT* xrow = reinterpret_cast<const XT*>(p.x) + (size_t)m * p.K;
         float mx = 0.0f;
         int bad = 0;
-        scan_groups<XT, 2>(p.pro, xrow, p.K, p.norm_w, rms, 0, p.K >> 2, sid, kSqThreads, mx, bad);
+        scan_groups<XT, 2>(kProNone, xrow, p.K, nullptr, 1.0f, 0, p.K >> 2, sid, kSqThreads, mx, bad);
         if (lane == 0) {
             s_red[sw] = mx;
             s_red[kSqWarps + sw] = __int_as_float(bad);
@@ -434,8 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* s_red = reinterpret_cast<float*>(s_exps + kMaxTokens);                   // [16] exponent reduction
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(                 // [kMaxTokens] argmax keys
         (reinterpret_cast<uintptr_t>(s_red + 2 * kSqWarps) + 7) & ~static_cast<uintptr_t>(7));
-    double* s_sq = reinterpret_cast<double*>(s_best + kMaxTokens);                      // [8] sum-of-squares partials
-    float* s_rms = reinterpret_cast<float*>(s_sq + kSqWarps);                               // [kMaxTokens] rms per token
 
     const uint32_t bar0 = tc::smem_u32(bars);
     const uint32_t full0 = bar0, dfull0 = bar0 + 8u * S, empty0 = bar0 + 16u * S, accfull0 = bar0 + 24u * S,
@@ -572,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed (the epilogue reads them too)
         // The per-token exponents into shared memory, by the epilogue and digitizer warps together:
         // found here for few tokens, else folded from the prep kernel's words.
-        if (p.fused_exps) fused_scan<XT>(p, 128 + dtid, s_exps, s_rms, s_red, s_sq);
+        if (p.fused_exps) fused_scan<XT>(p, 128 + dtid, s_exps, s_red);
         else fold_prep<XT>(p, 128 + dtid, s_exps);
         const int* exps = s_exps;
         sk::Ring st;
@@ -597,8 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
                     if (k < p.K && e != INT_MIN) {
                         float v[4];
-                        const float rms = p.pro == kProRmsNorm ? s_rms[m] : 1.0f;  // in-kernel prologue only
-                        act4<XT>(p.pro, xg + (size_t)m * p.ldx, p.K, k, p.norm_w, rms, v);
+                        load4<XT>(xg + (size_t)m * p.K + k, v);
 #pragma unroll
                         for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
                     }
@@ -627,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed
         // the per-token exponents, once per CTA, with the digitizer warps (they are read for every output)
-        if (p.fused_exps) fused_scan<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_rms, s_red, s_sq);
+        if (p.fused_exps) fused_scan<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_red);
         else fold_prep<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps);
         const int q = warp & 3;
         const int r = q * 32 + lane;
@@ -919,10 +895,6 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     p.amax_keys = a.amax_keys;
     p.amax_done = a.amax_done;
     p.amax_out = a.amax_out;
-    p.pro = a.prologue;
-    p.norm_w = a.norm_w;
-    p.eps = a.eps;
-    p.ldx = a.prologue == kProSiluMul ? 2 * (long long)a.K : (long long)a.K;
     p.ws = reinterpret_cast<int*>(sc.ws);
     p.counters = sc.counter_ptr;
     p.M = (int)a.M;
@@ -944,17 +916,12 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     const unsigned int prep_wait_seq = p.fused_exps ? 0u : p.po.wait_seq;
     if (!p.fused_exps) p.po.wait_seq = 0;
     const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
-    // A prologue without in-kernel exponents: the prep kernel writes the activations, the GEMV
-    // reads them as plain x.
-    const bool materialize = a.prologue != kProNone && !p.fused_exps;
+    // A prologue: the prep kernel writes the activations once, the GEMV reads them as plain x.
+    const bool materialize = a.prologue != kProNone;
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
         sc.exps_count < a.M * (size_t)ns || (materialize && sc.act_bytes < a.M * a.K * sizeof(XT)))
         return cudaErrorMemoryAllocation;
-    if (materialize) {
-        p.x = sc.act;
-        p.pro = kProNone;
-        p.ldx = (long long)a.K;
-    }
+    if (materialize) p.x = sc.act;
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)ns), dim3(kSqThreads), 0, stream, a.pdl,
@@ -982,10 +949,9 @@ int gemv_i8_max_tokens() { return kMaxTokens; }
 
 bool gemv_i8_fused_exps(const LinearArgs& a)
 {
-    if (a.M > (size_t)kFusedExpTokens) return false;
-    const bool small = a.N * a.K <= kPrologueInKernelMaxBytes;
-    if (a.prologue == kProNone) return a.K <= kFusedExpMaxK || (small && a.K <= kFusedExpMaxKSmall);
-    return a.K <= kFusedExpMaxK && small;
+    // A prologue is applied by the prep kernel, which writes the activations once.
+    if (a.M > (size_t)kFusedExpTokens || a.prologue != kProNone) return false;
+    return a.K <= kFusedExpMaxK || (a.N * a.K <= kInKernelScanMaxBytes && a.K <= kFusedExpMaxKSmall);
 }
 
 bool gemv_i8_supports(const LinearArgs& a)
