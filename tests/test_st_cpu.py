@@ -92,6 +92,9 @@ BAD_HEADERS = [
     ("bad escape", b'{"a\\q":{"dtype":"I8","shape":[1],"data_offsets":[0,1]}}', b"\0"),
     ("lone surrogate", b'{"a\\udc00":{"dtype":"I8","shape":[1],"data_offsets":[0,1]}}', b"\0"),
     ("deep", b"[" * 100 + b"]" * 100, b""),
+    ("bad utf-8", b'{"a\xff":{"dtype":"I8","shape":[1],"data_offsets":[0,1]}}', b"\0"),
+    ("overlong utf-8", b'{"\xc0\xaf":{"dtype":"I8","shape":[1],"data_offsets":[0,1]}}', b"\0"),
+    ("utf-8 surrogate", b'{"\xed\xa0\x80":{"dtype":"I8","shape":[1],"data_offsets":[0,1]}}', b"\0"),
 ]
 
 
@@ -134,3 +137,46 @@ def test_escapes_and_unicode_names(tmp_path):
     with v.SafeTensors(p) as f:
         assert f.names() == [name]
         assert f.tensor(name).tolist() == [5, 6]
+
+
+def test_header_fuzz_never_crashes(tmp_path):
+    """Seeded byte mutations of a valid header (flips, truncations, inserted bytes, changed
+    length word): every open either succeeds with consistent metadata or returns an error status."""
+    import random
+
+    import vvllm_b200 as v
+
+    good = str(tmp_path / "good.safetensors")
+    st_util.write(good, {"a.weight": ("F32", np.arange(12, dtype=np.float32).reshape(3, 4)),
+                         "b": ("I8", np.arange(5, dtype=np.int8)), "c": ("BF16", np.ones((2, 2), np.uint16))},
+                  {"k": "v"})
+    raw = open(good, "rb").read()
+    (hlen,) = struct.unpack("<Q", raw[:8])
+    rng = random.Random(1234)
+    p = str(tmp_path / "fuzz.safetensors")
+    opened = failed = 0
+    for _ in range(400):
+        b = bytearray(raw)
+        op = rng.randrange(4)
+        if op == 0:  # flip bytes inside the header
+            for _ in range(rng.randint(1, 4)):
+                b[8 + rng.randrange(hlen)] = rng.randrange(256)
+        elif op == 1:  # truncate anywhere
+            b = b[:rng.randrange(len(b))]
+        elif op == 2:  # insert a byte into the header, keeping the length word
+            i = 8 + rng.randrange(hlen)
+            b[i:i] = bytes([rng.randrange(256)])
+        else:  # corrupt the length word
+            b[:8] = struct.pack("<Q", rng.choice([0, 1, hlen - 1, hlen + 1, 1 << 33, rng.randrange(1 << 64)]))
+        with open(p, "wb") as fh:
+            fh.write(bytes(b))
+        try:
+            with v.SafeTensors(p) as f:
+                for i in range(len(f)):
+                    name, _, shape, _, nb = f.info(i)
+                    assert nb >= 0 and isinstance(name, str)
+            opened += 1
+        except v.B200Q8Error as e:
+            assert e.status in (-1, -7)
+            failed += 1
+    assert failed > 0 and opened + failed == 400

@@ -95,6 +95,28 @@ private:
             s->push_back((char)(0x80 | (cp & 0x3F)));
         }
     }
+    // The rest of a UTF-8 sequence whose lead byte is c (already consumed): well-formed, shortest
+    // form, no surrogates, at most U+10FFFF.
+    bool utf8_tail(unsigned char c, std::string* out)
+    {
+        int n;
+        unsigned cp;
+        if (c >= 0xC2 && c <= 0xDF) { n = 1; cp = c & 0x1F; }
+        else if (c >= 0xE0 && c <= 0xEF) { n = 2; cp = c & 0x0F; }
+        else if (c >= 0xF0 && c <= 0xF4) { n = 3; cp = c & 0x07; }
+        else return false;
+        if (e_ - p_ < n) return false;
+        out->push_back((char)c);
+        for (int i = 0; i < n; i++) {
+            const unsigned char t = (unsigned char)*p_++;
+            if ((t & 0xC0) != 0x80) return false;
+            cp = (cp << 6) | (t & 0x3F);
+            out->push_back((char)t);
+        }
+        if ((n == 2 && cp < 0x800) || (n == 3 && cp < 0x10000) || cp > 0x10FFFF || (cp >= 0xD800 && cp < 0xE000))
+            return false;
+        return true;
+    }
     bool hex4(unsigned* v)
     {
         if (e_ - p_ < 4) return false;
@@ -118,6 +140,10 @@ private:
         while (p_ < e_ && *p_ != '"') {
             const unsigned char c = (unsigned char)*p_++;
             if (c < 0x20) return false;
+            if (c >= 0x80) {  // a UTF-8 sequence: JSON text must be valid UTF-8
+                if (!utf8_tail(c, out)) return false;
+                continue;
+            }
             if (c != '\\') {
                 out->push_back((char)c);
                 continue;
@@ -631,10 +657,17 @@ int b200q8_st_quantize(const char* src_path, const char* dst_path, int device, u
     }
     FILE* fp = fopen(dst_path, "wb");
     if (!fp) return fail(B200Q8_ERR_IO, "st_quantize: cannot create %s", dst_path);
-    struct FileGuard {
+    struct FileGuard {  // an incomplete output file is removed
         FILE* fp;
-        ~FileGuard() { if (fp) fclose(fp); }
-    } fg{fp};
+        const char* path;
+        ~FileGuard()
+        {
+            if (fp) {
+                fclose(fp);
+                unlink(path);
+            }
+        }
+    } fg{fp, dst_path};
     const uint64_t hlen = h.size();
     if ((st = write_all(fp, &hlen, 8, dst_path)) || (st = write_all(fp, h.data(), h.size(), dst_path))) return st;
     for (auto& o : outs) {
@@ -664,7 +697,10 @@ int b200q8_st_quantize(const char* src_path, const char* dst_path, int device, u
         }
     }
     fg.fp = nullptr;
-    if (fclose(fp) != 0) return fail(B200Q8_ERR_IO, "st_quantize: closing %s failed", dst_path);
+    if (fclose(fp) != 0) {
+        unlink(dst_path);
+        return fail(B200Q8_ERR_IO, "st_quantize: closing %s failed", dst_path);
+    }
     return B200Q8_OK;
 }
 
