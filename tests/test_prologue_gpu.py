@@ -5,8 +5,8 @@ vvllm runs rms_norm per token before q/k/v and gate_up (include/vvllm/model/tran
 135-144, :167-169) and silu_mul before down (:171-188).  Checked here:
 
 * the fused call equals the standalone op followed by the plain projection bit for bit, on
-  every path the dispatcher takes (prologue inside the digit GEMV with in-kernel exponents,
-  with the prep kernel, in 42-token groups; standalone kernel + fp16 GEMM for prefill);
+  every path the dispatcher takes (the SIMT GEMV applying it while staging x; the digit GEMV's
+  prep kernel, also in 42-token groups; the standalone kernel + fp16 GEMM for prefill);
 * the standalone ops against the CPU oracle's restatement of BackendCPU::rms_norm / silu_mul
   (pinned bit for bit to the reference by tests/test_oracle.py);
 * the fused call against the oracle chain (oracle op -> oracle linear_q8) within the path's
@@ -34,13 +34,12 @@ def _same(a, b):
     return np.array_equal(a.view(np.uint32), b.view(np.uint32)) or np.array_equal(a, b, equal_nan=True)
 
 
-# (M, N, K, in16, out16): decode with in-kernel exponents, prep kernel (M > 4, K > 4096 or weights
-# over 32 MiB),
-# fp32 42-token groups, fp16 prefill on the GEMM
+# (M, N, K, in16, out16): few tokens on small weights (SIMT), on weights over 48 MiB or more
+# tokens (digit GEMV + prep kernel), fp32 42-token groups, fp16 prefill on the GEMM
 RN_CASES = [
     (1, 4864, 896, True, True),
     (1, 896, 896, False, False),
-    (1, 12288, 3584, True, True),   # weights > 32 MiB: the prep kernel writes the activations
+    (1, 16384, 3584, True, True),   # weights > 48 MiB: the prep kernel writes the activations
     (4, 1152, 3584, False, True),
     (5, 640, 896, False, False),
     (9, 4864, 896, True, True),
@@ -90,7 +89,7 @@ SM_CASES = [
     (1, 896, 4864, True, True, True),
     (1, 3584, 18944, False, False, True),
     (3, 896, 1024, False, False, False),
-    (1, 10240, 4096, True, False, False),   # weights > 32 MiB with few tokens: prep kernel path
+    (1, 14336, 4096, True, False, False),   # weights > 48 MiB with few tokens: prep kernel path
     (2, 512, 4096, True, False, False),
     (45, 256, 1024, False, False, True),
     (64, 896, 4864, True, True, True),

@@ -178,7 +178,7 @@ int reset_scratch_counters(int dev)
 }
 
 // Weights up to this size with few tokens go to the SIMT GEMV under ALGO_AUTO.
-constexpr size_t kSimtMaxWeightBytes = (size_t)32 << 20;
+constexpr size_t kSimtMaxWeightBytes = (size_t)48 << 20;
 
 // pro / norm_w / eps: an elementwise prologue (prologue.cuh) that turns inp into the activations
 // -- fused into the int8 digit GEMV, or run first into scratch when the GEMM takes the shape.
@@ -224,11 +224,12 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
     a.out_dtype = out_dtype;
     a.pdl = true;
     cudaError_t e;
-    // Kernel choice (AUTO): up to 4 tokens on at most 32 MiB of weights -> the SIMT streaming GEMV
+    // Kernel choice (AUTO): up to 4 tokens on at most 48 MiB of weights -> the SIMT streaming GEMV
     // (the tensor-core kernels' fixed costs -- barrier and TMEM set-up, pipeline fill, stream-K
     // fixup, ~6 us -- exceed a few-MB projection's whole streaming time: measured on B200, one
-    // token, 896x896 2.5 vs 6.0 us, 896x4864 4.6 vs 9.6 us, 49152x576 12.2 vs 12.5 us, and a
-    // Qwen2.5-0.5B decode step 555 vs 1070 us); up to 16 tokens -> int8 tensor-core GEMV with
+    // token, 896x896 2.5 vs 6.0 us, 896x4864 4.6 vs 9.6 us, 49152x576 12.2 vs 12.5 us, a 7B down
+    // shard 1792x18944 (34 MB) 14.3 vs 16.4 us, and a Qwen2.5-0.5B decode step 555 vs 1070 us; the
+    // 7B down projection itself, 68 MB, is 23.3 vs 20.2 us); up to 16 tokens -> int8 tensor-core GEMV with
     // exact activation digits; more tokens with fp16 activations -> fp16 tensor-core GEMM
     // (weights dequantized into TMEM); more tokens with fp32 activations -> the digit kernel in
     // groups of up to 42 tokens.  Shapes the tensor-core kernels cannot take (K % 16 != 0,

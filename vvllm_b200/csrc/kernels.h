@@ -51,8 +51,9 @@ struct LinearArgs {
     unsigned long long* amax_keys = nullptr;
     unsigned int* amax_done = nullptr;
     int* amax_out = nullptr;
-    // int8 digit GEMV only: an elementwise prologue computed from x where the GEMV reads its
-    // activations (prologue.cuh; kProNone: x is the activation).  x is then the prologue's
+    // SIMT streaming GEMV and int8 digit GEMV: an elementwise prologue computed from x (the SIMT
+    // kernel while it stages x, the digit GEMV's prep kernel into scratch; prologue.cuh;
+    // kProNone: x is the activation).  x is then the prologue's
     // input: [M, K] for kProRmsNorm (norm_w [K], eps), [M, 2K] gate | up for kProSiluMul.
     int prologue = 0;
     const float* norm_w = nullptr;
@@ -131,7 +132,7 @@ cudaError_t launch_gather_permute(const void* src, void* dst, int elem_bytes, si
 
 // Standalone prologue (prologue.cuh) over M tokens: out[M, K] in `dtype` from x ([M, K] for
 // kProRmsNorm, [M, 2K] for kProSiluMul).  K % 4 == 0; x and out 8-byte (fp16) / 16-byte (fp32)
-// aligned.  Same arithmetic as the prologue fused into the digit GEMV.
+// aligned.  Same arithmetic as the prologue fused into the SIMT GEMV and the digit GEMV's prep.
 cudaError_t launch_prologue(int pro, const void* x, void* out, int dtype, const float* norm_w, float eps, size_t M,
                             size_t K, bool pdl, cudaStream_t stream);
 

@@ -1,6 +1,7 @@
 // prologue.cu -- standalone rms_norm / silu_mul over M tokens.
 //
-// The same arithmetic as the prologue the int8 digit GEMV computes in-kernel (prologue.cuh),
+// The same arithmetic (prologue.cuh) as the SIMT GEMV applies while it stages x and the digit
+// GEMV's prep kernel applies when it writes the activations,
 // for the projections that run on the fp16 tensor-core GEMM (prefill: the activations are
 // written once and the GEMM's TMA reads them) and for the b200q8_rms_norm / b200q8_silu_mul
 // entry points (vvllm Backend::rms_norm per token, Backend::silu_mul over gate_up rows:

@@ -13,7 +13,7 @@
 //
 // The sum of squares is taken by kSqThreads = 256 threads in one fixed order (double partials
 // over 4-element groups t, t+256, ...; an xor-shuffle tree per warp; the eight warps added in
-// order), by every kernel that needs a token's rms: the fused GEMV's scan, its prep kernel
+// order), by every kernel that needs a token's rms: the SIMT GEMV's x staging, the digit GEMV's prep kernel
 // and the standalone prologue kernel all get the same bits, so a fused projection equals
 // the standalone prologue followed by the plain projection exactly.
 #pragma once
