@@ -563,51 +563,86 @@ def main():
 
     # ---- end to end through the C ABI with host buffers -------------------------------------
     # Each step copies its activations in (one pinned host -> device copy of all three inputs)
-    # and its outputs out (one device -> pinned host copy of all three outputs).
+    # and its outputs out (one device -> pinned host copy of all three outputs).  At N = 1 the
+    # copies run on a copy stream, double-buffered and ordered by events, so step i's copies
+    # overlap its neighbours' projections, as a serving loop would run them; at N > 1 the outputs
+    # live in the one symmetric buffer every rank writes, so the steps run serially.  Input and
+    # output copies take separate streams: on one stream the next step's input copy would queue
+    # behind this step's wait for its projections, and the copies would serialise with them again.
     Ks = [K for (_, _, K, _, _, _, _) in shards]
+    nbuf = 2 if comm is None else 1
     h_in = torch.empty((sum(Ks),), dtype=torch.float16).pin_memory()
-    d_in_all = torch.empty((sum(Ks),), dtype=torch.float16, device=dev)
-    d_in, o = [], 0
+    o = 0
     for K, x in zip(Ks, xs):
         h_in[o:o + K].copy_(x.view(-1).cpu())
-        d_in.append(d_in_all[o:o + K].view(1, K))
         o += K
+    d_in_all = [torch.empty((sum(Ks),), dtype=torch.float16, device=dev) for _ in range(nbuf)]
+    d_in = [[d_in_all[b][o0:o0 + K].view(1, K) for o0, K in zip([sum(Ks[:i]) for i in range(len(Ks))], Ks)]
+            for b in range(nbuf)]
     if comm is None:
         Ns = [N for (_, N, _, _, _, _, _) in shards]
-        d_out_all = torch.empty((sum(Ns),), dtype=torch.float16, device=dev)
-        d_outs, o = [], 0
-        for N in Ns:
-            d_outs.append(d_out_all[o:o + N].view(1, N))
-            o += N
-        out_src = d_out_all
+        out_src = [torch.empty((sum(Ns),), dtype=torch.float16, device=dev) for _ in range(nbuf)]
+        d_outs = [[out_src[b][o0:o0 + N].view(1, N) for o0, N in zip([sum(Ns[:i]) for i in range(len(Ns))], Ns)]
+                  for b in range(nbuf)]
     else:
-        d_outs = p2p_outs
-        out_src = sym.view(torch.float16)
-    h_out = torch.empty(out_src.shape, dtype=torch.float16).pin_memory()
+        out_src = [sym.view(torch.float16)]
+        d_outs = [p2p_outs]
+    h_out = [torch.empty(out_src[0].shape, dtype=torch.float16).pin_memory() for _ in range(nbuf)]
     h2d = h_in.numel() * 2
-    d2h = h_out.numel() * 2
+    d2h = h_out[0].numel() * 2
+    in_stream = torch.cuda.Stream(device=dev) if comm is None else stream
+    out_stream = torch.cuda.Stream(device=dev) if comm is None else stream
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready = [ev() for _ in range(nbuf)]   # input copy b landed
+    out_done = [ev() for _ in range(nbuf)]   # output copy b read out (buffers b free again)
+    comp_done = [ev() for _ in range(nbuf)]  # projections of buffer b finished
 
     def e2e_step(it):
         ws = sets[it % copies]
-        d_in_all.copy_(h_in, non_blocking=True)
+        b = it % nbuf
+        if comm is None:
+            if it >= nbuf:
+                in_stream.wait_event(out_done[b])  # buffer b's previous step is fully done
+            with torch.cuda.stream(in_stream):
+                d_in_all[b].copy_(h_in, non_blocking=True)
+            in_ready[b].record(in_stream)
+            stream.wait_event(in_ready[b])
+        else:
+            d_in_all[b].copy_(h_in, non_blocking=True)
         for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
             q, s = ws[i]
             if comm is None:
-                v.linear_q8(d_outs[i], d_in[i], q, s, None, stream=stream)
+                v.linear_q8(d_outs[b][i], d_in[b][i], q, s, None, stream=stream)
             else:
-                v.linear_q8_sharded_p2p(comm, d_outs[i], d_in[i], q, s, None, N, stream=stream,
+                v.linear_q8_sharded_p2p(comm, d_outs[b][i], d_in[b][i], q, s, None, N, stream=stream,
                                         defer_wait=True)
-        if comm is not None:
+        if comm is None:
+            comp_done[b].record(stream)
+            out_stream.wait_event(comp_done[b])
+            with torch.cuda.stream(out_stream):
+                h_out[b].copy_(out_src[b], non_blocking=True)
+            out_done[b].record(out_stream)
+        else:
             comm.wait(stream)  # every gathered output complete before the copy out
-        h_out.copy_(out_src, non_blocking=True)
+            h_out[b].copy_(out_src[b], non_blocking=True)
+
+    def e2e_drain():
+        if comm is None:
+            for b in range(nbuf):
+                stream.wait_event(out_done[b])  # the last outputs are in host memory
 
     for it in range(args.warmup):
         e2e_step(it)
+    e2e_drain()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    if comm is None:  # no copy starts before the timed region
+        in_stream.wait_event(e0)
+        out_stream.wait_event(e0)
     for it in range(args.steps):
         e2e_step(it)
+    e2e_drain()
     e1.record(stream)
     barrier()
     e_ms = e0.elapsed_time(e1)
