@@ -564,7 +564,7 @@ def main():
     # ---- end to end through the C ABI with host buffers -------------------------------------
     # Each step copies its activations in (one pinned host -> device copy of all three inputs)
     # and its outputs out (one device -> pinned host copy of all three outputs).  At N = 1 the
-    # copies run on a copy stream, double-buffered and ordered by events, so step i's copies
+    # copies run on their own streams, double-buffered and ordered by events, so step i's copies
     # overlap its neighbours' projections, as a serving loop would run them; at N > 1 the outputs
     # live in the one symmetric buffer every rank writes, so the steps run serially.  Input and
     # output copies take separate streams: on one stream the next step's input copy would queue
