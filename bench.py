@@ -294,7 +294,8 @@ def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
         o 896 (+residual), gate|up 896->9728, down 4864->896 (+residual)}, tied lm_head
         896->151936; 494 MB of weights (> 2x L2).
     value = algorithmic bytes of the step (weights, scales, biases, activations, outputs and the
-    residual reads) / median device time of one replay."""
+    residual reads) / median device time of one replay.  "qkv_grouped": the same step with each
+    layer's q/k/v as one linear_q8_group call on one x (same byte count)."""
     import torch
 
     torch.manual_seed(2)
@@ -323,36 +324,51 @@ def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
         nbytes = sum(algo_bytes(N, K, 1, a, a) + (4 * N if hb else 0) + (a * N if res else 0)
                      for N, K, hb, res in shapes)
 
-        def run(calls):
-            for q, sc, b, x, out, res in calls:
+        def run(calls, grouped):
+            i = 0
+            while i < len(calls):
+                q, sc, b, x, out, res = calls[i]
+                if grouped and i % 6 == 0 and i + 3 <= len(calls) - 1:  # q, k, v of one layer
+                    grp = calls[i:i + 3]
+                    v.linear_q8_group([c[4] for c in grp], x, [c[0] for c in grp], [c[1] for c in grp],
+                                      [c[2] for c in grp] if bias_qkv else None, stream=stream)
+                    i += 3
+                    continue
                 if res:
                     v.linear_q8_add(out, x, q, sc, b, out, stream=stream)
                 else:
                     v.linear_q8(out, x, q, sc, b, stream=stream)
+                i += 1
 
-        graphs = []
-        for calls in sets:
-            for _ in range(warmup):
-                run(calls)
-            stream.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                run(calls)
-            graphs.append(g)
-        ms = []
-        with torch.cuda.stream(stream):
-            for i in range(iters * copies):
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a0.record(stream)
-                graphs[i % copies].replay()
-                a1.record(stream)
-                a1.synchronize()
-                ms.append(a0.elapsed_time(a1))
-        del graphs
-        t = statistics.median(ms)
+        def timed(grouped):
+            graphs = []
+            for calls in sets:
+                for _ in range(warmup):
+                    run(calls, grouped)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    run(calls, grouped)
+                graphs.append(g)
+            ms = []
+            with torch.cuda.stream(stream):
+                for i in range(iters * copies):
+                    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
+                    graphs[i % copies].replay()
+                    a1.record(stream)
+                    a1.synchronize()
+                    ms.append(a0.elapsed_time(a1))
+            del graphs
+            return statistics.median(ms)
+
+        t = timed(False)
         gbs = nbytes / (t * 1e-3) / 1e9
+        tg = timed(True)
         return {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "us": round(t * 1e3, 2),
-                "calls": len(shapes), "bytes": nbytes, "weight_copies": copies}
+                "calls": len(shapes), "bytes": nbytes, "weight_copies": copies,
+                "qkv_grouped": {"value": round(nbytes / (tg * 1e-3) / 1e9, 1), "us": round(tg * 1e3, 2),
+                                "calls": len(shapes) - 2 * layers}}
 
     return {"smollm135m_fp32": stack(30, 576, 192, 1536, 49152, False, False, 2),
             "qwen05b_fp16": stack(24, 896, 128, 4864, 151936, True, True, 1),

@@ -217,6 +217,23 @@ B200Q8_API int b200q8_silu_mul_linear_q8_add(void* out, int out_dtype, const voi
                                              const void* residual, size_t M, size_t N, size_t K,
                                              b200q8_stream_t stream);
 
+/* Up to B200Q8_MAX_GROUP projections of the same activations: the rms_norm + q / k / v
+ * sequence of vvllm's attention block (include/vvllm/model/transformer.h:134-144, which calls
+ * rms_norm_seq and then linear three times on norm_out).  Projection i:
+ *   outs[i] [M, Ns[i]] = linear_q8(rms_norm(x), weights[i] [Ns[i], K], scales[i], biases[i])
+ * with biases null (no bias anywhere) or biases[i] null for a projection without one, and
+ * norm_weight null for no norm (then x is used as is).  Ns[i] == 0 skips projection i.
+ * With M <= 4 and at most 48 MiB of weights in all, one SIMT launch stages (and normalizes) x
+ * once for every projection; otherwise the projections run one after another through the
+ * b200q8_linear_q8 dispatch (norm fused or materialized as for b200q8_rms_norm_linear_q8).
+ * Each output equals the one of the single-projection call on the same inputs to 1e-5
+ * normwise (fp32) / 2e-3 (fp16).  No vvllm counterpart as one call. */
+#define B200Q8_MAX_GROUP 4
+B200Q8_API int b200q8_linear_q8_group(int n, void* const* outs, int out_dtype, const void* x, int in_dtype,
+                                      const float* norm_weight, float eps, const int8_t* const* weights,
+                                      const float* const* scales, const float* const* biases, const size_t* Ns,
+                                      size_t M, size_t K, b200q8_stream_t stream);
+
 /* The elementwise ops alone, same arithmetic (vvllm Backend::rms_norm applied per token, as
  * rms_norm_seq does, src/model/transformer.cc:40-50; Backend::silu_mul over each gate_up row,
  * transformer.h:175-180): out [M, K] in dtype from x [M, K] / gate_up [M, 2K] in dtype. */

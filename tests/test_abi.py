@@ -67,6 +67,19 @@ def test_argument_errors_without_device():
     assert L.b200q8_shard_range(10, 2, 2, ctypes.byref(a), ctypes.byref(b)) == -1
     # comm with null handle
     assert L.b200q8_linear_q8_sharded(None, None, 0, None, 0, None, None, None, 1, 4, 4, None, None) == -1
+    # grouped projections: count out of range, null arrays, outputs overlapping x or each other
+    P = ctypes.c_void_p * 2
+    ns = (ctypes.c_size_t * 2)(4, 4)
+    w, s, o = P(3 << 20, 5 << 20), P(4 << 20, 6 << 20), P(1 << 20, 7 << 20)
+    assert L.b200q8_linear_q8_group(0, o, 0, 2 << 20, 0, None, 0.0, w, s, None, ns, 1, 16, None) == -1
+    assert L.b200q8_linear_q8_group(5, o, 0, 2 << 20, 0, None, 0.0, w, s, None, ns, 1, 16, None) == -1
+    assert L.b200q8_linear_q8_group(2, None, 0, 2 << 20, 0, None, 0.0, w, s, None, ns, 1, 16, None) == -1
+    assert L.b200q8_linear_q8_group(2, P((2 << 20) + 4, 7 << 20), 0, 2 << 20, 0, None, 0.0, w, s, None, ns, 1, 16,
+                                    None) == -1
+    assert b"overlap" in L.b200q8_last_error()
+    assert L.b200q8_linear_q8_group(2, P(1 << 20, (1 << 20) + 8), 0, 2 << 20, 0, None, 0.0, w, s, None, ns, 1, 16,
+                                    None) == -1
+    assert b"overlap" in L.b200q8_last_error()
 
 
 @pytest.mark.parametrize("N,G", [(152064, 8), (18944, 4), (3584, 2), (10, 4), (3, 4), (1, 1), (7, 3)])

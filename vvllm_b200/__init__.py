@@ -36,6 +36,7 @@ from ._lib import (  # noqa: F401
     ST_OTHER,
     rms_norm,
     rms_norm_linear_q8,
+    linear_q8_group,
     shard_range,
     silu_mul,
     silu_mul_linear_q8_add,

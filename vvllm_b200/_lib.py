@@ -66,6 +66,8 @@ _SIGS = {
     "b200q8_rms_norm": ([_vp, _vp, _int, _vp, ctypes.c_float, _sz, _sz, _vp], _int),
     "b200q8_silu_mul": ([_vp, _vp, _int, _sz, _sz, _vp], _int),
     "b200q8_quantize_per_channel_bf16": ([_vp, _sz, _sz, _vp, _vp, _vp], _int),
+    "b200q8_linear_q8_group": ([_int, _vp, _int, _vp, _int, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _sz, _sz, _vp],
+                               _int),
     "b200q8_st_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _int),
     "b200q8_st_close": ([_vp], _int),
     "b200q8_st_count": ([_vp, ctypes.POINTER(_sz)], _int),
@@ -185,6 +187,24 @@ def silu_mul_linear_q8_add(out, gate_up, w, scales, bias=None, residual=None, st
     _check(lib().b200q8_silu_mul_linear_q8_add(_addr(out), _dtype_code(out), _addr(gate_up), _dtype_code(gate_up),
                                                _addr(w), _addr(scales), _addr(bias), _addr(residual), M, N, K,
                                                _stream(stream)))
+
+
+def linear_q8_group(outs, x, weights, scales, biases=None, norm_weight=None, eps=1e-6, stream=None) -> None:
+    """outs[i][M,N_i] = linear_q8(rms_norm(x) if norm_weight is not None else x, weights[i], scales[i],
+    biases[i]) for up to 4 projections of the same x (one launch for few tokens)."""
+    n = len(weights)
+    if not (len(outs) == len(scales) == n) or (biases is not None and len(biases) != n):
+        raise ValueError("outs, weights, scales (and biases) must have the same length")
+    M, K = x.shape
+    arr_p = ctypes.c_void_p * n
+    outs_a = arr_p(*[_addr(o) for o in outs])
+    w_a = arr_p(*[_addr(w) for w in weights])
+    s_a = arr_p(*[_addr(s) for s in scales])
+    b_a = arr_p(*[_addr(b) for b in biases]) if biases is not None else None
+    ns = (ctypes.c_size_t * n)(*[w.shape[0] for w in weights])
+    odt = _dtype_code(outs[0])
+    _check(lib().b200q8_linear_q8_group(n, outs_a, odt, _addr(x), _dtype_code(x), _addr(norm_weight), float(eps),
+                                        w_a, s_a, b_a, ns, M, K, _stream(stream)))
 
 
 def rms_norm(out, x, norm_weight, eps, stream=None) -> None:

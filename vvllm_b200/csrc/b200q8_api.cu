@@ -627,6 +627,89 @@ int b200q8_silu_mul_linear_q8_add(void* out, int out_dtype, const void* gate_up,
                        (cudaStream_t)stream, B200Q8_ALGO_AUTO, kProSiluMul);
 }
 
+int b200q8_linear_q8_group(int n, void* const* outs, int out_dtype, const void* x, int in_dtype,
+                           const float* norm_weight, float eps, const int8_t* const* weights,
+                           const float* const* scales, const float* const* biases, const size_t* Ns, size_t M,
+                           size_t K, b200q8_stream_t stream)
+{
+    if (n < 1 || n > B200Q8_MAX_GROUP)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_group: n must be 1..%d (n=%d)", B200Q8_MAX_GROUP, n);
+    if (!outs || !weights || !scales || !Ns) return fail(B200Q8_ERR_INVALID, "linear_q8_group: null array");
+    if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype))
+        return fail(B200Q8_ERR_INVALID, "linear_q8_group: dtype must be B200Q8_F32 or B200Q8_F16");
+    if (M == 0) return B200Q8_OK;
+    if (!x) return fail(B200Q8_ERR_INVALID, "linear_q8_group: null x");
+    if (K == 0 || K > (size_t)INT32_MAX || M > (size_t)INT32_MAX)
+        return fail(B200Q8_ERR_INVALID, "linear_q8_group: bad sizes (M=%zu K=%zu)", M, K);
+    const int pro = norm_weight ? kProRmsNorm : kProNone;
+    if (pro != kProNone) {
+        const size_t al = in_dtype == B200Q8_F16 ? 8 : 16;
+        if ((uintptr_t)norm_weight % 16)
+            return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_group: norm_weight must be 16-byte aligned");
+        if (K % 4 != 0 || (uintptr_t)x % al)
+            return fail(B200Q8_ERR_UNSUPPORTED, "linear_q8_group: the norm needs K %% 4 == 0 and a %zu-byte aligned x",
+                        al);
+    }
+    const size_t ob = out_dtype == B200Q8_F16 ? 2 : 4, ib = in_dtype == B200Q8_F16 ? 2 : 4;
+    const int8_t* w[kMaxGroup];
+    const float* s[kMaxGroup];
+    const float* b[kMaxGroup];
+    void* o[kMaxGroup];
+    size_t nn[kMaxGroup];
+    int live = 0;
+    size_t wbytes = 0;
+    for (int i = 0; i < n; i++) {
+        if (Ns[i] == 0) continue;
+        if (!outs[i] || !weights[i] || !scales[i])
+            return fail(B200Q8_ERR_INVALID, "linear_q8_group: null out/weight/scales of projection %d", i);
+        if (Ns[i] > (size_t)INT32_MAX || Ns[i] * K / K != Ns[i])
+            return fail(B200Q8_ERR_INVALID, "linear_q8_group: sizes overflow (N[%d]=%zu K=%zu)", i, Ns[i], K);
+        const uintptr_t o0 = (uintptr_t)outs[i], o1 = o0 + M * Ns[i] * ob;
+        const uintptr_t i0 = (uintptr_t)x, i1 = i0 + M * K * ib;
+        if (o0 < i1 && i0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8_group: x overlaps out %d", i);
+        for (int j = 0; j < live; j++) {
+            const uintptr_t p0 = (uintptr_t)o[j], p1 = p0 + M * nn[j] * ob;
+            if (o0 < p1 && p0 < o1) return fail(B200Q8_ERR_INVALID, "linear_q8_group: outputs overlap");
+        }
+        w[live] = weights[i];
+        s[live] = scales[i];
+        b[live] = biases ? biases[i] : nullptr;
+        o[live] = outs[i];
+        nn[live] = Ns[i];
+        wbytes += Ns[i] * K;
+        live++;
+    }
+    if (live == 0) return B200Q8_OK;
+    // Few tokens on a few MB of weights: one streaming launch that stages x (and normalizes it)
+    // once for every projection.  Otherwise, or for shapes that kernel does not take, one
+    // projection at a time through the ordinary dispatch.
+    if (live > 1 && M <= (size_t)gemv_max_tokens() && wbytes <= kSimtMaxWeightBytes) {
+        DeviceInfo d;
+        int st = device_info(&d);
+        if (st) return st;
+        LinearArgs a;
+        a.x = x;
+        a.M = M;
+        a.K = K;
+        a.in_dtype = in_dtype;
+        a.out_dtype = out_dtype;
+        a.pdl = true;
+        a.prologue = pro;
+        a.norm_w = norm_weight;
+        a.eps = eps;
+        const cudaError_t e = launch_q8_gemv_group(a, live, w, s, b, o, nn, d.num_sms, d.max_smem,
+                                                   (cudaStream_t)stream);
+        if (e == cudaSuccess) return B200Q8_OK;
+        if (e != cudaErrorNotSupported) return cuda_fail(e, "q8_gemv group launch");
+    }
+    for (int i = 0; i < live; i++) {
+        const int st = linear_impl(o[i], out_dtype, x, in_dtype, w[i], s[i], b[i], nullptr, M, nn[i], K,
+                                   (cudaStream_t)stream, B200Q8_ALGO_AUTO, pro, norm_weight, eps);
+        if (st) return st;
+    }
+    return B200Q8_OK;
+}
+
 }  // extern "C"
 
 // ===========================================================================

@@ -72,6 +72,15 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
 // The streaming SIMT kernel takes the shape (aligned, K % 16 == 0, M <= 4, x fits in shared
 // memory); only then may a.prologue be set (it is applied while x is staged).
 bool gemv_stream_supports(const LinearArgs& a, size_t max_smem);
+
+// A group of up to kMaxGroup projections of the same x in one SIMT launch (x staged, and its
+// prologue applied, once per CTA): matrix i is w[i] [Ns[i], a.K] with scales[i] and bias[i] (or
+// null) into outs[i] [a.M, Ns[i]] in a.out_dtype (a.w, a.out, a.res and a.N are not used).
+// cudaErrorNotSupported when the stream kernel cannot take the shapes or pointers.
+constexpr int kMaxGroup = 4;  // B200Q8_MAX_GROUP
+cudaError_t launch_q8_gemv_group(const LinearArgs& a, int n, const int8_t* const* w, const float* const* scales,
+                                 const float* const* bias, void* const* outs, const size_t* Ns, int num_sms,
+                                 size_t max_smem, cudaStream_t stream);
 int gemv_max_tokens();
 size_t gemv_smem_bytes(int M, int K);
 

@@ -52,7 +52,29 @@ struct GemvParams {
     int pro;             // prologue applied while x is staged (prologue.cuh); x rows are ldx apart
     const float* norm_w;
     float eps;
+    // The streaming kernel reads its matrices from these arrays: nmat projections of the same x
+    // (1 for a single one, where [0] repeats w / scales / bias / out / N above), matrix i with
+    // Nm[i] rows, its own weights, scales, bias and [M, Nm[i]] output, and row groups
+    // gofs[i] .. gofs[i+1] (gofs set at launch).
+    int nmat;
+    const int8_t* wm[kMaxGroup];
+    const float* sm[kMaxGroup];
+    const float* bm[kMaxGroup];
+    void* om[kMaxGroup];
+    int Nm[kMaxGroup];
+    int gofs[kMaxGroup + 1];
 };
+
+// The matrix row group g belongs to.  Only this index and the group's offset stay in registers
+// across the streaming loop; the matrix's pointers are read from the parameters where used.
+__device__ __forceinline__ int group_matrix(const GemvParams& p, int g)
+{
+    int i = 0;
+#pragma unroll
+    for (int j = 1; j < kMaxGroup; j++)
+        if (j < p.nmat && g >= p.gofs[j]) i = j;
+    return i;
+}
 static_assert(kThreads == kSqThreads, "the prologue's fixed-order sum is taken by one 256-thread CTA");
 
 template <typename XT>
@@ -173,16 +195,18 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
     const int c_begin = (int)((long long)kw * C / KW);
     const int c_end = (int)((long long)(kw + 1) * C / KW);
     const int rows_per_cta = RW * R;
-    const int num_groups = (p.N + rows_per_cta - 1) / rows_per_cta;
+    // a group of projections numbers its row groups matrix by matrix (offsets set at launch)
+    const int num_groups = p.gofs[p.nmat];
 
     // The weights do not depend on the previous kernel in the stream, x does: pull this CTA's
     // first row group (one contiguous range of rows_per_cta rows, 16-byte aligned on this path)
     // into L2 while that kernel finishes, then wait.
     if (threadIdx.x == 0 && (int)blockIdx.x < num_groups) {
-        const int r0 = (int)blockIdx.x * rows_per_cta;
-        const int nr = min(rows_per_cta, p.N - r0);
+        const int mi = group_matrix(p, (int)blockIdx.x);
+        const int r0 = ((int)blockIdx.x - p.gofs[mi]) * rows_per_cta;
+        const int nr = min(rows_per_cta, p.Nm[mi] - r0);
         const unsigned bytes = (unsigned)((long long)nr * p.K);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.w + (long long)r0 * p.K), "r"(bytes)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wm[mi] + (long long)r0 * p.K), "r"(bytes)
                      : "memory");
     }
     pdl_wait();
@@ -193,17 +217,17 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
     __syncthreads();
     pdl_launch_dependents();
 
-    const OT* res = reinterpret_cast<const OT*>(p.res);
-    OT* out = reinterpret_cast<OT*>(p.out);
+    const OT* res = reinterpret_cast<const OT*>(p.res);  // single projections only (ldo = N)
 
     int iter = 0;
     for (int g = blockIdx.x; g < num_groups; g += gridDim.x, iter++) {
-        const int row0 = g * rows_per_cta + rw * R;
+        const int mi = group_matrix(p, g);
+        const int row0 = (g - p.gofs[mi]) * rows_per_cta + rw * R;
         const int8_t* wrow[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            const int row = min(row0 + r, p.N - 1);  // tail rows re-read a valid row; never stored
-            wrow[r] = p.w + (long long)row * p.K;
+            const int row = min(row0 + r, p.Nm[mi] - 1);  // tail rows re-read a valid row; never stored
+            wrow[r] = p.wm[mi] + (long long)row * p.K;
         }
 
         float2 acc[MT][R][2];
@@ -258,10 +282,10 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
 #pragma unroll
                 for (int r = 0; r < R; r++) {
                     const int row = row0 + r;
-                    if (lane == t * R + r && t < p.M && row < p.N) {
-                        const long long o = (long long)t * p.ldo + row;
-                        epilogue_store<OT>(out + o, res ? res + o : nullptr, v[t][r], p.scales[row],
-                                           p.bias, row);
+                    if (lane == t * R + r && t < p.M && row < p.Nm[mi]) {
+                        const long long o = (long long)t * p.Nm[mi] + row;
+                        epilogue_store<OT>(reinterpret_cast<OT*>(p.om[mi]) + o, res ? res + o : nullptr, v[t][r],
+                                           p.sm[mi][row], p.bm[mi], row);
                     }
                 }
         } else {
@@ -277,13 +301,13 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
             if (kw == 0 && lane < MT * R) {
                 const int t = lane / R, r = lane % R;
                 const int row = row0 + r;
-                if (t < p.M && row < p.N) {
+                if (t < p.M && row < p.Nm[mi]) {
                     const float* base = red + ((iter & 1) * kWarps + rw * KW) * (MT * R);
                     float s = 0.f;
                     for (int k = 0; k < KW; k++) s += base[k * (MT * R) + lane];
-                    const long long o = (long long)t * p.ldo + row;
-                    epilogue_store<OT>(out + o, res ? res + o : nullptr, s, p.scales[row], p.bias,
-                                       row);
+                    const long long o = (long long)t * p.Nm[mi] + row;
+                    epilogue_store<OT>(reinterpret_cast<OT*>(p.om[mi]) + o, res ? res + o : nullptr, s,
+                                       p.sm[mi][row], p.bm[mi], row);
                 }
             }
         }
@@ -365,10 +389,13 @@ cudaError_t launch_stream_kernel(const GemvParams& p, int num_sms, cudaStream_t 
     const int per_sm = c.per_sm;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const int rows_per_cta = (kWarps / p.KW) * R;
-    const long long groups = (p.N + rows_per_cta - 1) / rows_per_cta;
+    GemvParams pg = p;  // row groups numbered matrix by matrix
+    pg.gofs[0] = 0;
+    for (int i = 0; i < p.nmat; i++) pg.gofs[i + 1] = pg.gofs[i] + (p.Nm[i] + rows_per_cta - 1) / rows_per_cta;
+    const long long groups = pg.gofs[p.nmat];
     long long grid = (long long)per_sm * num_sms;
     if (groups < grid) grid = groups;
-    return launch(kern, dim3((unsigned)grid), dim3(kThreads), smem, stream, p, pdl);
+    return launch(kern, dim3((unsigned)grid), dim3(kThreads), smem, stream, pg, pdl);
 }
 
 template <typename XT, typename OT>
@@ -438,6 +465,12 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
     p.pro = a.prologue;
     p.norm_w = a.norm_w;
     p.eps = a.eps;
+    p.nmat = 1;
+    p.wm[0] = p.w;
+    p.sm[0] = p.scales;
+    p.bm[0] = p.bias;
+    p.om[0] = p.out;
+    p.Nm[0] = p.N;
     const bool x16 = (a.in_dtype == kF16);
     const bool o16 = (a.out_dtype == kF16);
     if (gemv_stream_supports(a, max_smem)) {
@@ -451,6 +484,51 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
                         : dispatch_generic<__half, float>(p, stream, a.pdl);
     return o16 ? dispatch_generic<float, __half>(p, stream, a.pdl)
                : dispatch_generic<float, float>(p, stream, a.pdl);
+}
+
+cudaError_t launch_q8_gemv_group(const LinearArgs& a, int n, const int8_t* const* w, const float* const* scales,
+                                 const float* const* bias, void* const* outs, const size_t* Ns, int num_sms,
+                                 size_t max_smem, cudaStream_t stream)
+{
+    if (n < 1 || n > kMaxGroup) return cudaErrorInvalidValue;
+    LinearArgs b = a;
+    size_t total = 0;
+    for (int i = 0; i < n; i++) {
+        b.w = w[i];
+        if (!gemv_stream_supports(b, max_smem) || Ns[i] == 0 || Ns[i] > (size_t)INT32_MAX) return cudaErrorNotSupported;
+        total += Ns[i];
+    }
+    if (total > (size_t)INT32_MAX) return cudaErrorNotSupported;
+    GemvParams p{};
+    p.x = a.x;
+    p.w = w[0];
+    p.scales = scales[0];
+    p.bias = bias[0];
+    p.res = nullptr;
+    p.out = outs[0];
+    p.ldx = a.prologue == kProSiluMul ? 2 * (long long)a.K : (long long)a.K;
+    p.ldo = (long long)Ns[0];
+    p.N = (int)total;  // the dispatch heuristics see the group's rows
+    p.K = (int)a.K;
+    p.M = (int)a.M;
+    p.KW = 1;
+    p.pro = a.prologue;
+    p.norm_w = a.norm_w;
+    p.eps = a.eps;
+    p.nmat = n;
+    for (int i = 0; i < n; i++) {
+        p.wm[i] = w[i];
+        p.sm[i] = scales[i];
+        p.bm[i] = bias[i];
+        p.om[i] = outs[i];
+        p.Nm[i] = (int)Ns[i];
+    }
+    const bool x16 = (a.in_dtype == kF16);
+    const bool o16 = (a.out_dtype == kF16);
+    if (x16) return o16 ? dispatch_typed<__half, __half>(p, num_sms, stream, a.pdl)
+                        : dispatch_typed<__half, float>(p, num_sms, stream, a.pdl);
+    return o16 ? dispatch_typed<float, __half>(p, num_sms, stream, a.pdl)
+               : dispatch_typed<float, float>(p, num_sms, stream, a.pdl);
 }
 
 }  // namespace b200q8
