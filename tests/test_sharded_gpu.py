@@ -2,9 +2,10 @@
 
 Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range), runs
 b200q8_linear_q8_sharded, and must end with the full [M, N] output.  Checked
-against the unsharded single-GPU result (the int8 digit GEMV sums exact
-integers, so sharding cannot change its result) and against the CPU oracle on
-a row sample.
+against the unsharded single-GPU result on the same int8 digit GEMV (it sums exact integers, so
+sharding cannot change its result; the AUTO dispatch would pick the SIMT GEMV for the small
+unsharded shapes, whose float sums differ in the last bit) and against the CPU oracle on a row
+sample.
 """
 import os
 import socket
@@ -88,9 +89,9 @@ def _worker(rank, world, port, path):
             del bufs
             comm.sym_free(sym)
             del sym
-        if rank == 0:  # the unsharded result on one GPU
+        if rank == 0:  # the unsharded result on one GPU, on the digit GEMV the fused gather runs per shard
             full = torch.empty((M, N), dtype=torch.float16, device=dev)
-            v.linear_q8(full, xt, torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev))
+            v.linear_q8_ex(full, xt, torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev), algo=v.ALGO_TC_I8)
             fullf = torch.empty((M, N), dtype=torch.float32, device=dev)
             v.linear_q8_ex(fullf, xt.float(), torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev),
                            algo=v.ALGO_TC_I8)
@@ -122,8 +123,10 @@ def _worker(rank, world, port, path):
         if rank == 0:
             f1 = torch.empty((M, N1), dtype=torch.float16, device=dev)
             f2 = torch.empty((M, N2), dtype=torch.float16, device=dev)
-            v.linear_q8(f1, x, torch.from_numpy(data["q1"]).to(dev), torch.from_numpy(data["s1"]).to(dev))
-            v.linear_q8(f2, f1, torch.from_numpy(data["q2"]).to(dev), torch.from_numpy(data["s2"]).to(dev))
+            v.linear_q8_ex(f1, x, torch.from_numpy(data["q1"]).to(dev), torch.from_numpy(data["s1"]).to(dev),
+                           algo=v.ALGO_TC_I8)
+            v.linear_q8_ex(f2, f1, torch.from_numpy(data["q2"]).to(dev), torch.from_numpy(data["s2"]).to(dev),
+                           algo=v.ALGO_TC_I8)
             torch.cuda.synchronize()
             results[f"chainref{ci}"] = f2.float().cpu().numpy()
         del y1, y2
