@@ -28,9 +28,10 @@
 //              the previous kernel);
 //   warp 1     TMEM allocator + one thread issuing BK/32 kind::i8 MMAs per stage;
 //   warps 2-5  epilogue: tcgen05.ld, digit recombination, stores / fixup;
-//   warps 6-9  digitizers: read x for the stage (after the prep kernel's
-//              per-token exponents are ready), write the six digit rows per
-//              token straight into the stage's swizzled B tile in shared memory.
+//   warps 6-9  digitizers: read x for the stage (fp32: after the per-token
+//              exponents are ready; fp16 uses the fixed exponent), write the six
+//              digit rows per token straight into the stage's swizzled B tile in
+//              shared memory.
 // A prep kernel (one CTA per token) computes the exponents and flags rows with
 // Inf/NaN (their outputs are NaN).  Every mbarrier wait is bounded; a timeout
 // sets a device error word, drains in-flight copies and MMAs, frees TMEM and
@@ -292,13 +293,15 @@ __global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restric
     part[(size_t)m * ns + sp] = b_all ? -1 : __float_as_int(m_all);
 }
 
-// The prep kernel's words folded into the tokens' exponents in shared memory, by the epilogue
-// and digitizer warps together (sid 0..255, named barrier 3): warp w takes tokens w, w+8, ...
-template <typename XT>
+// The prep kernel's words folded into the tokens' exponents in shared memory by NT threads
+// (sid 0..NT-1) that meet at named barrier BAR: warp w takes tokens w, w + NT/32, ...
+// fp32: the epilogue and digitizer warps together (256, barrier 3); fp16, whose digits use the
+// fixed exponent: the epilogue warps alone (128, barrier 2).
+template <typename XT, int NT, int BAR>
 __device__ __forceinline__ void fold_prep(const DigParams& p, int sid, int* s_exps)
 {
     const int sw = sid >> 5, lane = sid & 31;
-    for (int m = sw; m < p.M; m += kSqWarps) {
+    for (int m = sw; m < p.M; m += NT / 32) {
         int hi = 0, lo = 0;
         for (int j = lane; j < p.prep_splits; j += 32) {
             const int v = p.prep_part[(size_t)m * p.prep_splits + j];
@@ -312,36 +315,38 @@ __device__ __forceinline__ void fold_prep(const DigParams& p, int sid, int* s_ex
         }
         if (lane == 0) s_exps[m] = token_exp<XT>(__int_as_float(hi), lo < 0 ? 1 : 0);
     }
-    asm volatile("bar.sync 3, 256;" ::: "memory");
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
 }
 
-// The exponents of a few tokens, computed inside the GEMV by its epilogue and digitizer warps
-// together (sid 0..255, named barrier 3), with the prep kernel's rules.
-template <typename XT>
+// The exponents of a few tokens, computed inside the GEMV with the prep kernel's rules by NT
+// threads (sid 0..NT-1) that meet at named barrier BAR, as for fold_prep.
+template <typename XT, int NT, int BAR>
 __device__ __forceinline__ void fused_scan(const DigParams& p, int sid, int* s_exps, float* s_red)
 {
+    constexpr int NW = NT / 32;
+    static_assert(NW <= kSqWarps, "s_red holds 2 * kSqWarps words");
     const int sw = sid >> 5, lane = sid & 31;
 #pragma unroll 1
     for (int m = 0; m < p.M; m++) {
         const XT* xrow = reinterpret_cast<const XT*>(p.x) + (size_t)m * p.K;
         float mx = 0.0f;
         int bad = 0;
-        scan_groups<XT, 2>(kProNone, xrow, p.K, nullptr, 1.0f, 0, p.K >> 2, sid, kSqThreads, mx, bad);
+        scan_groups<XT, NT == 128 ? 4 : 2>(kProNone, xrow, p.K, nullptr, 1.0f, 0, p.K >> 2, sid, NT, mx, bad);
         if (lane == 0) {
             s_red[sw] = mx;
             s_red[kSqWarps + sw] = __int_as_float(bad);
         }
-        asm volatile("bar.sync 3, 256;" ::: "memory");
+        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
         if (sid == 0) {
             float m_all = 0.0f;
             int b_all = 0;
-            for (int i = 0; i < kSqWarps; i++) {
+            for (int i = 0; i < NW; i++) {
                 m_all = fmaxf(m_all, s_red[i]);
                 b_all |= __float_as_int(s_red[kSqWarps + i]);
             }
             s_exps[m] = token_exp<XT>(m_all, b_all);
         }
-        asm volatile("bar.sync 3, 256;" ::: "memory");
+        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
     }
 }
 
@@ -547,10 +552,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed (the epilogue reads them too)
-        // The per-token exponents into shared memory, by the epilogue and digitizer warps together:
-        // found here for few tokens, else folded from the prep kernel's words.
-        if (p.fused_exps) fused_scan<XT>(p, 128 + dtid, s_exps, s_red);
-        else fold_prep<XT>(p, 128 + dtid, s_exps);
+        // fp32: the per-token exponents into shared memory, by the epilogue and digitizer warps
+        // together (found here for few tokens, else folded from the prep kernel's words).  fp16
+        // digits use the fixed exponent, so the digitizers start at once; the epilogue warps find
+        // the tokens holding Inf/NaN (their outputs are NaN; their digits are never used).
+        if constexpr (sizeof(XT) != 2) {
+            if (p.fused_exps) fused_scan<XT, 256, 3>(p, 128 + dtid, s_exps, s_red);
+            else fold_prep<XT, 256, 3>(p, 128 + dtid, s_exps);
+        }
         const int* exps = s_exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
@@ -570,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int m = item / (BK / 4);
                     const int kk = (item - m * (BK / 4)) * 4;  // 0..BK-4
                     const int k = kb * BK + kk;
-                    const int e = exps[m];
+                    const int e = sizeof(XT) == 2 ? kF16Exp : exps[m];
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
                     if (k < p.K && e != INT_MIN) {
                         float v[4];
@@ -602,9 +611,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.po.wait_seq)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed
-        // the per-token exponents, once per CTA, with the digitizer warps (they are read for every output)
-        if (p.fused_exps) fused_scan<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_red);
-        else fold_prep<XT>(p, threadIdx.x - kFirstEpi * 32, s_exps);
+        // the per-token exponents, once per CTA (read for every output): fp32 with the digitizer
+        // warps; fp16 (only the Inf/NaN flags) by these warps alone while the digits stream
+        if constexpr (sizeof(XT) == 2) {
+            if (p.fused_exps) fused_scan<XT, 128, 2>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_red);
+            else fold_prep<XT, 128, 2>(p, threadIdx.x - kFirstEpi * 32, s_exps);
+        } else {
+            if (p.fused_exps) fused_scan<XT, 256, 3>(p, threadIdx.x - kFirstEpi * 32, s_exps, s_red);
+            else fold_prep<XT, 256, 3>(p, threadIdx.x - kFirstEpi * 32, s_exps);
+        }
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
@@ -951,6 +966,8 @@ bool gemv_i8_fused_exps(const LinearArgs& a)
 {
     // A prologue is applied by the prep kernel, which writes the activations once.
     if (a.M > (size_t)kFusedExpTokens || a.prologue != kProNone) return false;
+    // fp16: the scan (Inf/NaN flags only) is the epilogue warps' alone, off the digits' path
+    if (a.in_dtype == kF16 && a.M == 1 && a.K <= kFusedExpMaxKSmall) return true;
     return a.K <= kFusedExpMaxK || (a.N * a.K <= kInKernelScanMaxBytes && a.K <= kFusedExpMaxKSmall);
 }
 
