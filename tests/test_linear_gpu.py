@@ -188,6 +188,36 @@ def test_i8_nonfinite_rows_give_nan(cuda, oracle):
         assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32
 
 
+# (M, N, K, position of the bad value): fp16 rows scanned in-kernel for one token up to 20480
+# wide and for up to 4 tokens up to 4096 wide; from the prep kernel's words otherwise
+FP16_BAD = [
+    (1, 256, 896, -3),
+    (1, 512, 18944, -1),     # 7B down width, one token: in-kernel, by the epilogue warps alone
+    (1, 384, 24576, 0),      # wider: prep kernel, folded by the epilogue warps alone
+    (2, 256, 896, 100),
+    (3, 320, 8192, -5),      # several tokens on long rows: prep kernel
+]
+
+
+@pytest.mark.parametrize("M,N,K,pos", FP16_BAD)
+@pytest.mark.parametrize("val", [np.inf, np.nan])
+def test_i8_fp16_nonfinite_rows_give_nan(cuda, oracle, M, N, K, pos, val):
+    """fp16 digits use the fixed exponent; only the epilogue warps look for Inf/NaN. The token
+    holding one gets NaN outputs, wherever in the row it sits, and the others match the oracle."""
+    import vvllm_b200 as v
+
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 130 + K % 97))
+    x = make_x(M, K, 131 + M)
+    bad = M // 2
+    x[bad, pos] = val
+    y, xe, _ = run_gpu(cuda, x, q, s, None, None, in16=True, algo=v.ALGO_TC_I8)
+    assert np.all(np.isnan(y[bad]))
+    ref = oracle_ref(oracle, xe, q, s, None, None)
+    for i in range(M):
+        if i != bad:
+            assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F16, i
+
+
 def test_i8_prep_kernel_scratch_across_token_counts(cuda, oracle):
     """Rows longer than 4096 take the prep kernel, several CTAs per token combining through
     zero-at-rest words in the per-stream scratch.  Calls with different token counts in a row
