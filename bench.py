@@ -471,14 +471,17 @@ def main():
         dist.broadcast_object_list(uid, src=0)
         comm = v.Comm(local, world, rank, uid[0], timeout_s=120.0)
         # Outputs of the fused gather: [1, N] fp16 each, in one symmetric allocation that
-        # every peer has mapped (256-byte aligned slots).
+        # every peer has mapped (256-byte aligned slots); two sets of slots, one per step parity
+        # of the end-to-end leg (the timed loop uses set 0).
         offs, o = [], 0
         for (_, N, _, _, _, _, _) in shards:
             offs.append(o)
             o += -(-N * 2 // 256) * 256
-        sym = comm.sym_alloc(o)
-        p2p_outs = [sym[a:a + 2 * N].view(torch.float16).view(1, N)
-                    for a, (_, N, _, _, _, _, _) in zip(offs, shards)]
+        sym = comm.sym_alloc(2 * o)
+        sym_sets = [[sym[h * o + a:h * o + a + 2 * N].view(torch.float16).view(1, N)
+                     for a, (_, N, _, _, _, _, _) in zip(offs, shards)] for h in range(2)]
+        sym_src = [sym[h * o:(h + 1) * o].view(torch.float16) for h in range(2)]
+        p2p_outs = sym_sets[0]
 
     stream = torch.cuda.current_stream()
     lm_idx = [n for n, *_ in PROJ].index("lm_head")
@@ -579,14 +582,17 @@ def main():
 
     # ---- end to end through the C ABI with host buffers -------------------------------------
     # Each step copies its activations in (one pinned host -> device copy of all three inputs)
-    # and its outputs out (one device -> pinned host copy of all three outputs).  At N = 1 the
-    # copies run on their own streams, double-buffered and ordered by events, so step i's copies
-    # overlap its neighbours' projections, as a serving loop would run them; at N > 1 the outputs
-    # live in the one symmetric buffer every rank writes, so the steps run serially.  Input and
-    # output copies take separate streams: on one stream the next step's input copy would queue
-    # behind this step's wait for its projections, and the copies would serialise with them again.
+    # and its outputs out (one device -> pinned host copy of all three outputs).  The copies run
+    # on their own streams, double-buffered and ordered by events, so step i's copies overlap its
+    # neighbours' projections, as a serving loop would run them.  Input and output copies take
+    # separate streams: on one stream the next step's input copy would queue behind this step's
+    # wait for its projections, and the copies would serialise with them again.  At N > 1 the
+    # outputs are two sets of symmetric slots that the peers write: a peer runs at most one
+    # gathered call ahead of this rank (each call waits for every rank's part of the previous
+    # one), so holding this rank's last call of step i + 1 until step i's outputs are in host
+    # memory keeps every peer off that set until then.
     Ks = [K for (_, _, K, _, _, _, _) in shards]
-    nbuf = 2 if comm is None else 1
+    nbuf = 2
     h_in = torch.empty((sum(Ks),), dtype=torch.float16).pin_memory()
     o = 0
     for K, x in zip(Ks, xs):
@@ -601,13 +607,13 @@ def main():
         d_outs = [[out_src[b][o0:o0 + N].view(1, N) for o0, N in zip([sum(Ns[:i]) for i in range(len(Ns))], Ns)]
                   for b in range(nbuf)]
     else:
-        out_src = [sym.view(torch.float16)]
-        d_outs = [p2p_outs]
+        out_src = sym_src
+        d_outs = sym_sets
     h_out = [torch.empty(out_src[0].shape, dtype=torch.float16).pin_memory() for _ in range(nbuf)]
     h2d = h_in.numel() * 2
     d2h = h_out[0].numel() * 2
-    in_stream = torch.cuda.Stream(device=dev) if comm is None else stream
-    out_stream = torch.cuda.Stream(device=dev) if comm is None else stream
+    in_stream = torch.cuda.Stream(device=dev)
+    out_stream = torch.cuda.Stream(device=dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
     in_ready = [ev() for _ in range(nbuf)]   # input copy b landed
     out_done = [ev() for _ in range(nbuf)]   # output copy b read out (buffers b free again)
@@ -616,36 +622,34 @@ def main():
     def e2e_step(it):
         ws = sets[it % copies]
         b = it % nbuf
-        if comm is None:
-            if it >= nbuf:
-                in_stream.wait_event(out_done[b])  # buffer b's previous step is fully done
-            with torch.cuda.stream(in_stream):
-                d_in_all[b].copy_(h_in, non_blocking=True)
-            in_ready[b].record(in_stream)
-            stream.wait_event(in_ready[b])
-        else:
+        if it >= nbuf:
+            in_stream.wait_event(out_done[b])  # buffer b's previous step is fully done
+        with torch.cuda.stream(in_stream):
             d_in_all[b].copy_(h_in, non_blocking=True)
+        in_ready[b].record(in_stream)
+        stream.wait_event(in_ready[b])
         for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
             q, s = ws[i]
             if comm is None:
                 v.linear_q8(d_outs[b][i], d_in[b][i], q, s, None, stream=stream)
             else:
+                if i == len(shards) - 1 and it >= 1:
+                    # the other set's outputs (step it - 1) are in host memory before this call
+                    # lets any peer start step it + 1 into that set
+                    stream.wait_event(out_done[(it - 1) % nbuf])
                 v.linear_q8_sharded_p2p(comm, d_outs[b][i], d_in[b][i], q, s, None, N, stream=stream,
                                         defer_wait=True)
-        if comm is None:
-            comp_done[b].record(stream)
-            out_stream.wait_event(comp_done[b])
-            with torch.cuda.stream(out_stream):
-                h_out[b].copy_(out_src[b], non_blocking=True)
-            out_done[b].record(out_stream)
-        else:
+        if comm is not None:
             comm.wait(stream)  # every gathered output complete before the copy out
+        comp_done[b].record(stream)
+        out_stream.wait_event(comp_done[b])
+        with torch.cuda.stream(out_stream):
             h_out[b].copy_(out_src[b], non_blocking=True)
+        out_done[b].record(out_stream)
 
     def e2e_drain():
-        if comm is None:
-            for b in range(nbuf):
-                stream.wait_event(out_done[b])  # the last outputs are in host memory
+        for b in range(nbuf):
+            stream.wait_event(out_done[b])  # the last outputs are in host memory
 
     for it in range(args.warmup):
         e2e_step(it)
@@ -653,9 +657,8 @@ def main():
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    if comm is None:  # no copy starts before the timed region
-        in_stream.wait_event(e0)
-        out_stream.wait_event(e0)
+    in_stream.wait_event(e0)  # no copy starts before the timed region
+    out_stream.wait_event(e0)
     for it in range(args.steps):
         e2e_step(it)
     e2e_drain()
@@ -728,7 +731,7 @@ def main():
 
     if comm is not None:
         torch.cuda.synchronize()
-        del p2p_outs, sym, d_outs, out_src
+        del p2p_outs, sym_sets, sym_src, sym, d_outs, out_src
         comm.destroy()
     if world > 1:
         dist.destroy_process_group()
