@@ -96,3 +96,23 @@ def test_shard_range_partitions_rows(N, G):
     assert nxt == N
     if N % G == 0:
         assert all(n == N // G for _, n in got)
+
+
+def test_group_binding_checks_shapes_and_dtypes():
+    """The Python group binding refuses mixed output dtypes and mis-shaped buffers before any call."""
+    import torch
+
+    import vvllm_b200 as v
+
+    x = torch.zeros((2, 64))
+    w = [torch.zeros((8, 64), dtype=torch.int8), torch.zeros((4, 64), dtype=torch.int8)]
+    s = [torch.zeros(8), torch.zeros(4)]
+    with pytest.raises(ValueError, match="dtype"):
+        v.linear_q8_group([torch.zeros((2, 8)), torch.zeros((2, 4), dtype=torch.float16)], x, w, s)
+    with pytest.raises(ValueError, match="projection 1"):
+        v.linear_q8_group([torch.zeros((2, 8)), torch.zeros((2, 5))], x, w, s)
+    with pytest.raises(ValueError, match="projection 0"):
+        v.linear_q8_group([torch.zeros((2, 8)), torch.zeros((2, 4))], x,
+                          [torch.zeros((8, 32), dtype=torch.int8), w[1]], s)
+    with pytest.raises(ValueError, match="same length"):
+        v.linear_q8_group([torch.zeros((2, 8))], x, w, s)

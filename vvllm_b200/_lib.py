@@ -196,6 +196,11 @@ def linear_q8_group(outs, x, weights, scales, biases=None, norm_weight=None, eps
     if not (len(outs) == len(scales) == n) or (biases is not None and len(biases) != n):
         raise ValueError("outs, weights, scales (and biases) must have the same length")
     M, K = x.shape
+    for i, (o, w) in enumerate(zip(outs, weights)):
+        if o.dtype != outs[0].dtype:
+            raise ValueError(f"outs[{i}] is {o.dtype}, outs[0] is {outs[0].dtype}: one output dtype per group")
+        if tuple(w.shape) != (w.shape[0], K) or tuple(o.shape) != (M, w.shape[0]) or not o.is_contiguous():
+            raise ValueError(f"projection {i}: weights must be [N, {K}] and outs [{M}, N] contiguous")
     arr_p = ctypes.c_void_p * n
     outs_a = arr_p(*[_addr(o) for o in outs])
     w_a = arr_p(*[_addr(w) for w in weights])
