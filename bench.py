@@ -17,6 +17,13 @@ HBM bytes moved per second (int8 weights + fp32 scales + activations in +
 outputs out, summed over ranks), timed on the device with CUDA events over K
 steps, max over ranks.  Weight sets rotate so one cycle per rank exceeds 2x
 the 126 MB L2 (inputs larger than L2).  Output: one JSON line on rank 0.
+
+Beside the headline, the line carries: a parity verdict (N = 1: the reference's
+own CPU linear_q8 on a row sample of every projection; N > 1: every rank's
+gathered outputs against the unsharded digit GEMV of each rank's rows, bit for
+bit); BASELINE configs 1-4 and config 5 at M = 8 and 64 (rank 0, N = 1); the
+GPU quantize against the reference's single-threaded quantize_per_channel; and
+the reference's CPU linear_q8 on working sets larger than twice the host's LLC.
 """
 from __future__ import annotations
 
@@ -61,16 +68,13 @@ def algo_bytes(N: int, K: int, M: int = 1, a: int = 2, o: int = 2) -> int:
 
 
 def profiled_traffic(kernel: str):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"{kernel}.md")
+    """DRAM bytes per launch of the dominant kernel (dram__bytes_read.sum + dram__bytes_write.sum
+    of one ncu capture), from profiles/roofline_traffic.json, if recorded."""
     try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return int(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            return int(json.load(f)[kernel]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
 
 
 class ClockSampler:
@@ -82,8 +86,8 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
-        self.samples, self.reasons = [], 0
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], 0  # samples: (time, SM MHz, reason bits)
         self.period = period_s
         self._stop = threading.Event()
         self.ok = False
@@ -102,8 +106,10 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.monotonic(), mhz, r))
+                self.reasons |= r
             except Exception:
                 pass
             time.sleep(self.period)
@@ -119,12 +125,25 @@ class ClockSampler:
         if self.ok:
             self.t.join()
 
-    def summary(self):
+    def _names(self, bits):
+        return [n for bit, n in self.REASONS.items() if bits & bit and n != "gpu_idle"]
+
+    def summary(self, window=None):
+        """Median SM clock and the clock-event reasons seen, over the whole sampled run and over
+        `window` = (t0, t1) (time.monotonic()), the timed region."""
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
-        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
-                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(m for _, m, _ in self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": self._names(self.reasons), "samples": len(self.samples),
+               "period_ms": self.period * 1e3, "covers": "warm-up through the last GPU leg of the run"}
+        if window is not None:
+            inside = [(m, r) for t, m, r in self.samples if window[0] <= t <= window[1]]
+            bits = 0
+            for _, r in inside:
+                bits |= r
+            out["timed_region"] = {"sm_mhz": statistics.median(m for m, _ in inside) if inside else None,
+                                   "samples": len(inside), "reasons": self._names(bits)}
+        return out
 
 
 def cpu_info():
@@ -149,6 +168,35 @@ def cpu_reference_lib():
     return Oracle(), "port"
 
 
+def llc_bytes() -> int:
+    """Size of the host's largest CPU cache level (sysfs), 0 if unknown."""
+    best = 0
+    base = "/sys/devices/system/cpu/cpu0/cache"
+    try:
+        names = os.listdir(base)
+    except OSError:
+        return 0
+    for d in names:
+        if not d.startswith("index"):
+            continue
+        try:
+            with open(os.path.join(base, d, "size")) as f:
+                txt = f.read().strip()
+            mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}.get(txt[-1:], 1)
+            best = max(best, int(txt.rstrip("KMG")) * mult)
+        except (OSError, ValueError):
+            continue
+    return best
+
+
+def cpu_sample_bytes(requested_mb: float) -> int:
+    """int8 weight bytes the CPU legs stream per pass: as requested, else twice the host's LLC
+    (at least 64 MB), so the reference reads its weights from DRAM as in the real workload."""
+    if requested_mb > 0:
+        return int(requested_mb * 1e6)
+    return max(2 * llc_bytes(), 64 << 20)
+
+
 def time_cpu_linear(lib, shapes, threads: int, budget_s: float, min_iters: int = 1):
     """Times lib.linear_q8_mt over `shapes` (list of (x, q, s)); returns (GB/s, seconds/iter, iters)."""
     total_bytes = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
@@ -165,17 +213,22 @@ def time_cpu_linear(lib, shapes, threads: int, budget_s: float, min_iters: int =
     return total_bytes * iters / el / 1e9, el / iters, iters
 
 
-def host_sample_weights(frac_rows: float, seed: int = 0):
-    """Host int8 weights for a row sample of every projection (values do not change CPU timing)."""
+def host_sample_weights(min_bytes: int, seed: int = 0):
+    """Host int8 weights for the same fraction of every projection's rows, at least `min_bytes` in
+    all (values do not change the CPU's timing: random bytes repeated from an 8 MB block).
+    Returns (list of (x, q, s), fraction of the rows)."""
+    total = sum(N * K for _, N, K in PROJ)
+    frac = min(1.0, max(min_bytes / total, 1e-3))
     rng = np.random.default_rng(seed)
+    block = rng.integers(-127, 128, size=1 << 23, dtype=np.int8)
     out = []
     for name, N, K in PROJ:
-        n = max(1, int(N * frac_rows))
-        q = rng.integers(-127, 128, size=(n, K), dtype=np.int8)
+        n = max(1, int(math.ceil(N * frac)))
+        q = np.resize(block, n * K).reshape(n, K)
         s = (rng.random(n, dtype=np.float32) * np.float32(1e-3)).astype(np.float32)
         x = rng.standard_normal((1, K), dtype=np.float32).astype(np.float16).astype(np.float32)
         out.append((x, q, s))
-    return out
+    return out, frac
 
 
 def run_reference(args):
@@ -185,8 +238,7 @@ def run_reference(args):
         return 0
     lib, kind = cpu_reference_lib()
     model, cores = cpu_info()
-    frac = args.cpu_sample
-    shapes = host_sample_weights(frac)
+    shapes, frac = host_sample_weights(cpu_sample_bytes(args.cpu_sample_mb))
     sample_bytes = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
     for _ in range(args.warmup):
         for x, q, s in shapes:
@@ -199,21 +251,42 @@ def run_reference(args):
         times.append(time.perf_counter() - t0)
     el = sum(times)
     gbs = sample_bytes * args.steps / el / 1e9
-    sample = (f"{frac:.3f} of the rows of each projection ({sample_bytes / 1e6:.1f} MB algorithmic per step), "
-              f"fp32 activations widened from fp16, {cores} threads on disjoint output-channel slices; "
-              f"CPU: {model}")
+    sample = (f"{frac:.3f} of the rows of each projection ({sample_bytes / 1e6:.1f} MB algorithmic per step, "
+              f"> 2x the host's {llc_bytes() / 2**20:.0f} MiB LLC), fp32 activations widened from fp16, "
+              f"{cores} threads on disjoint output-channel slices; CPU: {model}")
     line = {
         "metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * el / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8 weights x f32 activations, f32 accumulate",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": "cpu threads"},
+        "data": "synthetic", "config": {"workload": WORKLOAD, "M": 1, "parallelism": "cpu threads"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_quantize(lib, min_bytes: int, budget_s: float):
+    """The reference's quantize_per_channel, one thread (as the reference runs it at model load),
+    on a [R, 3584] fp32 matrix of at least `min_bytes`; bytes = 4NK read + NK + 4N written."""
+    K = HIDDEN
+    R = max(1024, int(math.ceil(min_bytes / (4 * K))))
+    rng = np.random.default_rng(5)
+    block = (rng.standard_normal(1 << 22, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    w = np.resize(block, R * K).reshape(R, K)
+    lib.quantize_per_channel(w[:256])  # warm the code
+    iters, t0 = 0, time.perf_counter()
+    while True:
+        lib.quantize_per_channel(w)
+        iters += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    nbytes = 5 * R * K + 4 * R
+    return {"value": round(nbytes * iters / el / 1e9, 3), "unit": "GB/s", "cores": 1,
+            "sample": f"[{R}, {K}] fp32 ({4 * R * K / 1e6:.0f} MB in), {iters} pass(es) in {el:.1f} s"}
 
 
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N), M = 512
@@ -375,6 +448,73 @@ def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
             "timing": "median CUDA-graph replay of one whole step (device time), weights cycled beyond L2"}
 
 
+def config1_gemv(v, dev, warmup: int, iters: int, hbm_peak: float):
+    """one fp32 decode GEMV, x [1, 896] -> y [1, 4864] (4.4 MB of int8 weights).
+    One CUDA graph runs the call once on each of enough weight copies to exceed 2x L2, so every
+    call streams its weights from HBM; per-call time = median replay time / copies."""
+    import torch
+
+    N, K = 4864, 896
+    torch.manual_seed(3)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    copies = int(math.ceil(2 * L2_BYTES / (N * K)))
+    ws = [(torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev), torch.rand(N, device=dev) * 1e-3)
+          for _ in range(copies)]
+    x = torch.randn(1, K, device=dev)
+    out = torch.empty(1, N, device=dev)
+    for _ in range(warmup):
+        for q, s in ws:
+            v.linear_q8(out, x, q, s, stream=stream)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for q, s in ws:
+            v.linear_q8(out, x, q, s, stream=stream)
+    ms = []
+    with torch.cuda.stream(stream):
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+    del g
+    t_call = statistics.median(ms) / copies
+    gbs = algo_bytes(N, K, 1, 4, 4) / (t_call * 1e-3) / 1e9
+    return {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "us_per_call": round(t_call * 1e3, 3),
+            "shape": "x fp32 [1, 896] -> y fp32 [1, 4864]", "weight_copies": copies,
+            "timing": "median CUDA-graph replay of one call per weight copy (copies > 2x L2), divided by copies"}
+
+
+def gpu_quantize(v, dev, iters: int, hbm_peak: float):
+    """The GPU quantize_per_channel on a [32768, 3584] fp32 matrix (470 MB in, > L2), median of
+    `iters` launches timed with events; bytes = 4NK read + NK + 4N written."""
+    import torch
+
+    R, K = 32768, HIDDEN
+    w = torch.randn(R, K, device=dev) * 0.02
+    q = torch.empty(R, K, dtype=torch.int8, device=dev)
+    s = torch.empty(R, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    v.quantize_per_channel(w, q, s, stream=stream)
+    ms = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        v.quantize_per_channel(w, q, s, stream=stream)
+        b.record(stream)
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+    t = statistics.median(ms)
+    nbytes = 5 * R * K + 4 * R
+    gbs = nbytes / (t * 1e-3) / 1e9
+    del w, q, s
+    return {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "us": round(t * 1e3, 2),
+            "shape": f"[{R}, {K}] fp32 -> int8 + fp32 scales"}
+
+
 def profile_case(args):
     """Small single-projection run for ncu: warmup + 1 launches of one linear_q8 on one GPU.
     Weights are random int8 made with one torch launch (values do not change the memory traffic)."""
@@ -408,8 +548,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--cpu-sample", type=float, default=0.125,
-                    help="fraction of each projection's rows timed on the CPU")
+    ap.add_argument("--cpu-sample-mb", type=float, default=0.0,
+                    help="int8 weight MB the CPU legs stream per pass (default: 2x the host's LLC, >= 64 MB)")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None,
@@ -512,6 +652,9 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    # SM clocks are sampled from the first warm-up step to the end of the last GPU leg.
+    sampler = ClockSampler(local)
+    sampler.__enter__()
     for it in range(args.warmup):
         step(it)
     if comm is not None:
@@ -522,18 +665,18 @@ def main():
     # itself a stream operation, so the next kernel could no longer start behind the previous
     # one (programmatic dependent launch) and the step would measure slower than it runs.
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    with sampler:
-        barrier()
-        n0 = v.launch_count()
-        t_start.record(stream)
-        for it in range(args.steps):
-            step(it)
-        if comm is not None:
-            comm.wait(stream)
-        t_end.record(stream)
-        barrier()
-        n_launch = v.launch_count() - n0
+    barrier()
+    win0 = time.monotonic()
+    n0 = v.launch_count()
+    t_start.record(stream)
+    for it in range(args.steps):
+        step(it)
+    if comm is not None:
+        comm.wait(stream)
+    t_end.record(stream)
+    barrier()
+    win1 = time.monotonic()
+    n_launch = v.launch_count() - n0
     ms = t_start.elapsed_time(t_end)
     # The lm_head roofline: the same K steps again, events around each lm_head launch (live, on
     # the launching stream; these events cost the steps their overlap, not the lm_head launch).
@@ -546,6 +689,26 @@ def main():
         comm.wait(stream)
     barrier()
     lm_ms = statistics.mean(a.elapsed_time(b) for a, b in lm_events)
+
+    # ---- N > 1 parity: every rank's gathered outputs (the last step's, in the symmetric buffers)
+    # ---- against each rank's rows computed locally by the same digit GEMV, gathered by NCCL ------
+    parity = None
+    if comm is not None:
+        same = 1
+        for i, (name, N, K, r0, rows, _, _) in enumerate(shards):
+            q, s = sets[0][i]
+            loc = torch.empty((1, per[i] * world), dtype=torch.float16, device=dev)
+            mine = loc[:, rank * per[i]:rank * per[i] + per[i]]
+            v.linear_q8_ex(mine[:, :rows], xs[i], q, s, algo=v.ALGO_TC_I8, stream=stream)
+            full = torch.empty((1, per[i] * world), dtype=torch.float16, device=dev)
+            dist.all_gather_into_tensor(full, mine.contiguous())
+            same &= int(torch.equal(full[:, :N], p2p_outs[i]))
+        flag = torch.tensor([same], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        parity = {"ok": bool(flag.item()), "ranks": world,
+                  "check": "every rank's gathered [1, N] outputs of the last timed step equal, bit for bit, "
+                           "each rank's rows computed by the unsharded digit GEMV (ALGO_TC_I8) and all-gathered "
+                           "by NCCL; the digit GEMV itself is checked against the reference in tests/"}
     if world > 1:
         t = torch.tensor([ms, lm_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -671,30 +834,86 @@ def main():
         e_ms = t.item()
     e2e_value = total_bytes / (e_ms / args.steps * 1e-3) / 1e9
 
-    # ---- prefill GEMM TFLOP/s (M = 512, fp16 in/out), rank 0 at N = 1 ------
-    prefill = stacks = None
+    # ---- BASELINE config 5 at M = 8 and 64 tokens, configs 1-4, and the GPU quantize (rank 0, N = 1) ----
+    prefill = stacks = cfg1 = quant = None
+    tokens = {}
     if world == 1:
+        for M in (8, 64):
+            xm = [torch.randn((M, K), generator=gen, device=dev).half() for (_, _, K, _, _, _, _) in shards]
+            om = [torch.empty((M, rows), dtype=torch.float16, device=dev) for (_, _, _, _, rows, _, _) in shards]
+
+            def tok_step(it, xm=xm, om=om):
+                ws = sets[it % copies]
+                for i in range(len(shards)):
+                    q, s = ws[i]
+                    v.linear_q8(om[i], xm[i], q, s, None, stream=stream)
+
+            nsteps = max(20, args.steps // 4)
+            for it in range(args.warmup):
+                tok_step(it)
+            barrier()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for it in range(nsteps):
+                tok_step(it)
+            c1.record(stream)
+            barrier()
+            t_step = c0.elapsed_time(c1) / nsteps
+            nb = sum(algo_bytes(N, K, M) for _, N, K in PROJ)
+            gbs = nb / (t_step * 1e-3) / 1e9
+            tokens[f"M{M}"] = {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                               "us_per_step": round(t_step * 1e3, 2),
+                               "TFLOP/s": round(sum(2.0 * M * N * K for _, N, K in PROJ) / (t_step * 1e-3) / 1e12, 1),
+                               "kernel": "q8_gemv_dig_kernel (int8 tensor cores)" if M <= 16
+                               else "q8_gemm_sk_kernel (fp16 tensor cores)"}
+            del xm, om
+        cfg1 = config1_gemv(v, dev, args.warmup, max(20, args.steps // 4), hbm_peak)
         prefill = prefill_tflops(v, dev, stream, args.warmup, max(5, args.steps // 10), tc_peak)
         stacks = decode_stacks(v, dev, args.warmup, max(10, args.steps // 10), hbm_peak)
+        quant = gpu_quantize(v, dev, max(5, args.steps // 20), hbm_peak)
+    sampler.__exit__(None, None, None)
 
-    # ---- CPU baseline: the reference's linear_q8 on the host cores (rank 0, N = 1) ------------
+    # ---- CPU baseline: the reference's linear_q8 on the host cores (rank 0, N = 1), and the
+    # ---- parity check of this run's outputs against it on a row sample of every projection ------
     cpu_baseline = None
     if world == 1 and not args.no_cpu_baseline:
         lib, kind = cpu_reference_lib()
         model, cores = cpu_info()
-        shapes = host_sample_weights(args.cpu_sample)
+        want = cpu_sample_bytes(args.cpu_sample_mb)
+        shapes, frac = host_sample_weights(want)
         gbs, sec, iters = time_cpu_linear(lib, shapes, cores, args.cpu_budget)
         sb = sum(algo_bytes(q.shape[0], q.shape[1], 1, 4, 4) for _, q, _ in shapes)
-        # the reference runs single-threaded: time that too, on a smaller row sample
-        shapes1 = host_sample_weights(args.cpu_sample / 8, seed=1)
-        gbs1, sec1, iters1 = time_cpu_linear(lib, shapes1, 1, args.cpu_budget / 2)
+        # the reference runs single-threaded: time that too, on the same working set
+        gbs1, sec1, iters1 = time_cpu_linear(lib, shapes, 1, args.cpu_budget / 2)
+        del shapes
+        cq = cpu_quantize(lib, want, args.cpu_budget / 2)
+        if quant is not None:
+            quant["cpu_reference_single_thread"] = cq
+        llc = llc_bytes()
         cpu_baseline = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-                        "sample": f"{args.cpu_sample:.3f} of each projection's rows "
-                                  f"({sb / 1e6:.1f} MB algorithmic), {iters} passes in {sec * iters:.1f} s, "
+                        "sample": f"{frac:.3f} of each projection's rows ({sb / 1e6:.1f} MB algorithmic, "
+                                  f"host LLC {llc / 2**20:.0f} MiB), {iters} passes in {sec * iters:.1f} s, "
                                   f"{cores} threads (disjoint output-row slices); CPU: {model}",
                         "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
-                                          "sample": f"{args.cpu_sample / 8:.4f} of each projection's rows, "
-                                                    f"{iters1} passes in {sec1 * iters1:.1f} s"}}
+                                          "sample": f"the same rows, {iters1} passes in {sec1 * iters1:.1f} s"}}
+        # parity: 64 sampled output channels of every projection (first, middle and last included),
+        # this run's GPU outputs of the last timed step against the reference's linear_q8 on the
+        # same int8 rows, scales and (fp16-widened) activations
+        worst = 0.0
+        for i, (name, N, K, r0, rows, q, s) in enumerate(shards):
+            pick = sorted(set(np.random.default_rng(11 + i).choice(N, size=61, replace=False).tolist())
+                          | {0, N // 2, N - 1})
+            idx = torch.tensor(pick, device=dev)
+            qh = q.index_select(0, idx).cpu().numpy()
+            sh = s.index_select(0, idx).cpu().numpy()
+            xh = xs[i].float().cpu().numpy()
+            ref = lib.linear_q8(xh, np.ascontiguousarray(qh), np.ascontiguousarray(sh), None)[0]
+            got = outs[i][0].index_select(0, idx).float().cpu().numpy()
+            den = float(np.max(np.abs(ref)))
+            worst = max(worst, float(np.max(np.abs(got - ref))) / den if den > 0 else float(np.max(np.abs(got))))
+        parity = {"ok": worst <= 2e-3, "max_normwise_err": worst, "tol": 2e-3,
+                  "check": f"64 output channels of each projection, this run's fp16 outputs against the {kind} "
+                           f"CPU linear_q8 on the same int8 rows and fp16-widened activations"}
 
     if rank == 0:
         traffic = profiled_traffic("q8_gemv_dig_lm_head_7b") if world == 1 else None
@@ -715,12 +934,19 @@ def main():
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms / args.steps, 5)},
             "gpu_launches": int(n_launch),
-            "clocks": sampler.summary(),
+            "clocks": sampler.summary((win0, win1)),
+            "parity": parity,
         }
         if compute_only is not None:
             line["compute_only"] = compute_only
         if nccl_leg is not None:
             line["gemv_then_nccl_allgather"] = nccl_leg
+        if tokens:
+            line["tokens"] = tokens
+        if cfg1 is not None:
+            line["config1_gemv_fp32"] = cfg1
+        if quant is not None:
+            line["quantize"] = quant
         if prefill is not None:
             line["prefill"] = prefill
         if stacks is not None:

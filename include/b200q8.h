@@ -248,6 +248,20 @@ B200Q8_API int b200q8_silu_mul(void* out, const void* gate_up, int dtype, size_t
  * clear != 0 resets it.  Synchronises with the device. */
 B200Q8_API int b200q8_kernel_error(int* code, int clear);
 
+/* Diagnostics (no vvllm counterpart): the bounded wait a gathered call makes for its peers'
+ * completion counts (b200q8_linear_q8_sharded_p2p), run on caller memory so that a failure test
+ * can make it run out on one GPU -- a count that nothing advances stands for a rank that never
+ * finished.  counts [n] (device uint64, 1 <= n <= 8) must each reach seq * 2^20 (wrapping
+ * compare) within timeout_s (0.001 .. 10 s); otherwise bit 1 of b200q8_kernel_error is set and
+ * the kernel returns.  where: 0 = the standalone wait kernel (what b200q8_comm_wait enqueues);
+ * 1 = inside the int8 digit GEMV before it reads x (how a deferred wait is paid; a give-up also
+ * sets bit 0 and the GEMV's outputs are invalid); 2 = inside that GEMV's per-token prep kernel.
+ * For 1 and 2 the GEMV out[1, N] = linear_q8(x[1, K], weight[N, K], scales) runs with fp16 x and
+ * out, exactly as b200q8_linear_q8_ex(..., B200Q8_ALGO_TC_I8) would. */
+B200Q8_API int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, double timeout_s, int where,
+                                     void* out, const void* x, const int8_t* weight, const float* scales, size_t N,
+                                     size_t K, b200q8_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * 2. Backend layer.  Mirrors vvllm::BackendCUDA's hot-path conventions:
  *    activations (out, inp, residual) are device pointers, fp32 or -- when the

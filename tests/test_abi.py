@@ -116,3 +116,27 @@ def test_group_binding_checks_shapes_and_dtypes():
                           [torch.zeros((8, 32), dtype=torch.int8), w[1]], s)
     with pytest.raises(ValueError, match="same length"):
         v.linear_q8_group([torch.zeros((2, 8))], x, w, s)
+    outs = [torch.zeros((2, 8)), torch.zeros((2, 4))]
+    with pytest.raises(ValueError, match="scales"):  # a short scales vector would be read past its end
+        v.linear_q8_group(outs, x, w, [s[0], torch.zeros(3)])
+    with pytest.raises(ValueError, match="bias"):
+        v.linear_q8_group(outs, x, w, s, [torch.zeros(8), torch.zeros(2)])
+    with pytest.raises(ValueError, match="x must be contiguous"):
+        v.linear_q8_group(outs, torch.zeros((64, 2)).t(), w, s)
+    with pytest.raises(ValueError, match="weights must be contiguous"):
+        v.linear_q8_group(outs, x, [w[0], torch.zeros((64, 4), dtype=torch.int8).t()], s)
+
+
+def test_diag_peer_wait_argument_errors():
+    """The failure-test entry point validates its arguments before any CUDA call."""
+    from vvllm_b200 import _lib
+
+    L = _lib.lib()
+    assert L.b200q8_diag_peer_wait(None, 1, 1, 0.1, 0, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 9, 1, 0.1, 0, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 0, 0.1, 0, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 20.0, 0, None, None, None, None, 0, 0, None) == -1
+    assert b"timeout" in L.b200q8_last_error()
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 0.1, 3, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 0.1, 1, None, None, None, None, 16, 16, None) == -1
+    assert b"GEMV needs" in L.b200q8_last_error()

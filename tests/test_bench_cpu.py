@@ -15,7 +15,7 @@ def _run(extra_env=None):
     env = dict(os.environ)
     env.update(extra_env or {})
     return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
-                           "--warmup", "1", "--cpu-sample", "0.004"], cwd=ROOT, env=env, capture_output=True,
+                           "--warmup", "1", "--cpu-sample-mb", "4"], cwd=ROOT, env=env, capture_output=True,
                           text=True, timeout=300)
 
 

@@ -1,4 +1,4 @@
-"""Column-sharded linear_q8 over 2 GPUs with the library's NCCL all-gather (needs >= 2 GPUs).
+"""Column-sharded linear_q8 over 2, 4 and 8 GPUs (each world size runs where that many GPUs exist).
 
 Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range), runs
 b200q8_linear_q8_sharded, and must end with the full [M, N] output.  Checked
@@ -139,13 +139,13 @@ def _worker(rank, world, port, path):
     dist.destroy_process_group()
 
 
-def test_sharded_two_gpus(tmp_path, oracle):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded(tmp_path, oracle, world):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     for ci, (M, N, K) in enumerate(CASES):
         q, s = oracle.quantize_per_channel(make_weight(N, K, 900 + ci))
         x = make_x(M, K, 910 + ci).astype(np.float16).astype(np.float32)

@@ -5,9 +5,10 @@ or budget nothing may bypass, or their decode loop cannot take the device-wide
 synchronisation cudaMalloc/cudaFree may cause.  For them the library offers one
 entry point whose scratch is a fixed device array.  This file checks, through
 the C ABI, that it gives the same results as the regular entry point
-(b200q8_linear_q8_ex), within the tolerances every other test uses, on two
-calls in a row (the second call reuses the array the first one left behind),
-and that shapes beyond the array's limits are refused.
+(b200q8_linear_q8_ex) and as the CPU oracle (the reference's linear_q8 /
+linear_q8_add on the same inputs), within the tolerances every other test
+uses, on two calls in a row (the second call reuses the array the first one
+left behind), and that shapes beyond the array's limits are refused.
 
 It is named to be collected last, so a run that stops at the first failure has
 run every other test before this one; it also passes alone in a fresh process.
@@ -60,8 +61,18 @@ def test_noalloc_matches_regular_entry_two_calls(cuda, oracle, M, N, K, in16, ha
         v.linear_q8_ex(want, x, qt, st, bt, res)
         torch.cuda.synchronize()
         assert v.kernel_error() == 0
-        err = rowwise_normwise_err(got.float().cpu().numpy(), want.float().cpu().numpy())
+        y = got.float().cpu().numpy()
+        err = rowwise_normwise_err(y, want.float().cpu().numpy())
         assert err <= tol, (call, err)
+        # and against the oracle on the same (widened) inputs
+        xf = x.float().cpu().numpy()
+        b = bt.cpu().numpy() if has_b else None
+        if has_r:
+            ref = oracle.linear_q8_add(xf, q, s, b, np.ascontiguousarray(res.float().cpu().numpy()))
+        else:
+            ref = oracle.linear_q8(xf, q, s, b)
+        err = rowwise_normwise_err(y, ref)
+        assert err <= tol, (call, "oracle", err)
 
 
 def test_noalloc_rejects_shapes_beyond_its_array(cuda):

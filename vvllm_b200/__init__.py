@@ -19,6 +19,7 @@ from ._lib import (  # noqa: F401
     linear_q8_argmax,
     linear_q8_ex,
     kernel_error,
+    diag_peer_wait,
     ALGO_AUTO,
     ALGO_SIMT,
     ALGO_TC,

@@ -36,6 +36,8 @@ _SIGS = {
     "b200q8_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_linear_q8_ex": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _int, _vp], _int),
     "b200q8_kernel_error": ([ctypes.POINTER(_int), _int], _int),
+    "b200q8_diag_peer_wait": ([_vp, _int, ctypes.c_uint, ctypes.c_double, _int, _vp, _vp, _vp, _vp, _sz, _sz, _vp],
+                              _int),
     "b200q8_linear_q8_noalloc": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_backend_create": ([_int, _int, ctypes.POINTER(_vp)], _int),
     "b200q8_backend_destroy": ([_vp], _int),
@@ -196,11 +198,20 @@ def linear_q8_group(outs, x, weights, scales, biases=None, norm_weight=None, eps
     if not (len(outs) == len(scales) == n) or (biases is not None and len(biases) != n):
         raise ValueError("outs, weights, scales (and biases) must have the same length")
     M, K = x.shape
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous [M, K]")
     for i, (o, w) in enumerate(zip(outs, weights)):
         if o.dtype != outs[0].dtype:
             raise ValueError(f"outs[{i}] is {o.dtype}, outs[0] is {outs[0].dtype}: one output dtype per group")
         if tuple(w.shape) != (w.shape[0], K) or tuple(o.shape) != (M, w.shape[0]) or not o.is_contiguous():
             raise ValueError(f"projection {i}: weights must be [N, {K}] and outs [{M}, N] contiguous")
+        if not w.is_contiguous():
+            raise ValueError(f"projection {i}: weights must be contiguous")
+        if scales[i].numel() != w.shape[0] or not scales[i].is_contiguous():
+            raise ValueError(f"projection {i}: scales must hold N = {w.shape[0]} contiguous values")
+        if biases is not None and biases[i] is not None and (biases[i].numel() != w.shape[0]
+                                                              or not biases[i].is_contiguous()):
+            raise ValueError(f"projection {i}: bias must hold N = {w.shape[0]} contiguous values")
     arr_p = ctypes.c_void_p * n
     outs_a = arr_p(*[_addr(o) for o in outs])
     w_a = arr_p(*[_addr(w) for w in weights])
@@ -323,6 +334,17 @@ def kernel_error(clear: bool = True) -> int:
     c = _int()
     _check(lib().b200q8_kernel_error(ctypes.byref(c), int(clear)))
     return c.value
+
+
+def diag_peer_wait(counts, seq: int, timeout_s: float, where: int = 0, out=None, x=None, w=None, scales=None,
+                   stream=None) -> None:
+    """The gathered calls' bounded peer wait on `counts` (uint64 / int64 device tensor of n words):
+    where 0 = the standalone wait kernel, 1 = inside the digit GEMV, 2 = inside its prep kernel
+    (1 and 2 run out[1, N] = linear_q8(x[1, K] fp16, w, scales) behind the wait).  A wait that runs
+    out is reported by kernel_error() (bit 1), not by this call."""
+    N, K = (w.shape[0], w.shape[1]) if w is not None else (0, 0)
+    _check(lib().b200q8_diag_peer_wait(_addr(counts), counts.numel(), seq, float(timeout_s), where, _addr(out),
+                                       _addr(x), _addr(w), _addr(scales), N, K, _stream(stream)))
 
 
 def shard_range(N: int, nranks: int, rank: int) -> tuple[int, int]:

@@ -466,8 +466,66 @@ int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* inp, int in_d
         case 4: return fail(B200Q8_ERR_UNSUPPORTED,
                             "linear_q8_noalloc: needs K %% 16 == 0, 16 <= K <= 131072, a 16-byte aligned weight and an "
                             "8-byte (fp16) / 16-byte (fp32) aligned input (K=%zu)", K);
+        case 5: return fail(B200Q8_ERR_UNSUPPORTED,
+                            "linear_q8_noalloc: M=%zu N=%zu K=%zu needs more scratch than the fixed array holds", M, N, K);
         default: return cuda_fail(e, "linear_q8_noalloc");
     }
+}
+
+// The bounded wait of the gathered calls, run on caller memory so that a test can make it run
+// out on one GPU (a count nothing advances) and see the status the host reads afterwards.
+int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, double timeout_s, int where, void* out,
+                          const void* x, const int8_t* weight, const float* scales, size_t N, size_t K,
+                          b200q8_stream_t stream)
+{
+    if (!counts || n < 1 || n > kMaxRanks || seq == 0)
+        return fail(B200Q8_ERR_INVALID, "diag_peer_wait: counts, 1 <= n <= %d and seq > 0 required", kMaxRanks);
+    if (!(timeout_s >= 1e-3 && timeout_s <= 10.0))
+        return fail(B200Q8_ERR_INVALID, "diag_peer_wait: timeout_s must lie in [0.001, 10]");
+    if (where < 0 || where > 2) return fail(B200Q8_ERR_INVALID, "diag_peer_wait: where must be 0, 1 or 2");
+    const unsigned long long ns = (unsigned long long)(timeout_s * 1e9);
+    const unsigned long long* cts = reinterpret_cast<const unsigned long long*>(counts);
+    cudaError_t e;
+    if (where == 0) {
+        e = launch_p2p_wait(cts, n, 0, seq, ns, (cudaStream_t)stream);
+        return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "diag_peer_wait: wait launch");
+    }
+    if (!out || !x || !weight || !scales || N == 0 || K == 0 || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX)
+        return fail(B200Q8_ERR_INVALID, "diag_peer_wait: the GEMV needs out, x, weight, scales, N and K");
+    DeviceInfo d;
+    int st = device_info(&d);
+    if (st) return st;
+    P2POut po;
+    po.ndst = 1;
+    po.dst[0] = out;
+    po.ldo = (long long)N;
+    po.wait_counts = cts;
+    po.wait_n = n;
+    po.wait_seq = seq;
+    po.wait_timeout_ns = ns;
+    LinearArgs a;
+    a.x = x;
+    a.w = weight;
+    a.scales = scales;
+    a.out = out;
+    a.M = 1;
+    a.N = N;
+    a.K = K;
+    a.in_dtype = B200Q8_F16;
+    a.out_dtype = B200Q8_F16;
+    a.pdl = true;
+    a.p2p = &po;
+    a.force_prep = where == 2;
+    if (!gemv_i8_supports(a))
+        return fail(B200Q8_ERR_UNSUPPORTED, "diag_peer_wait: the digit GEMV does not take K=%zu or these pointers", K);
+    if (where == 1 && !gemv_i8_fused_exps(a))
+        return fail(B200Q8_ERR_UNSUPPORTED, "diag_peer_wait: K=%zu is scanned by the prep kernel (use where=2)", K);
+    ScratchNeed need;
+    gemv_i8_scratch_need(a, d.num_sms, &need.ws, &need.counters, &need.act, &need.exps);
+    TcScratch scratch;
+    if ((st = get_scratch(need, d.num_sms, (cudaStream_t)stream, &scratch))) return st;
+    e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream);
+    return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "diag_peer_wait: GEMV launch");
 }
 
 int b200q8_linear_q8_argmax(void* out, int out_dtype, const void* inp, int in_dtype, const int8_t* weight,

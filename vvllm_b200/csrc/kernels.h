@@ -33,6 +33,7 @@ struct P2POut {
     const unsigned long long* wait_counts = nullptr;
     int wait_n = 0;
     unsigned int wait_seq = 0;
+    unsigned long long wait_timeout_ns = 0;  // limit of that wait (0: the default, 2 s)
 };
 
 struct LinearArgs {
@@ -58,6 +59,9 @@ struct LinearArgs {
     int prologue = 0;
     const float* norm_w = nullptr;
     float eps = 0.0f;
+    // int8 digit GEMV only: find the per-token exponents in the prep kernel even where the GEMV
+    // would scan x itself (lets a deferred peer wait be paid in the prep kernel on any shape).
+    bool force_prep = false;
 };
 
 // One thread waits (bounded, `timeout_ns`) until counts[j] has reached seq << kCountShift for
@@ -121,7 +125,7 @@ cudaError_t read_kernel_error_i8(int* code, bool clear);
 
 // The int8 digit GEMV on a fixed file-scope device array instead of allocated
 // scratch (see q8_gemv_tc.cu).  0: launched; 1..4: the shape exceeds the
-// array's limits (tokens, rows, SM count, K/alignment); -1: CUDA error in *err.
+// array's limits (tokens, rows, SM count, K/alignment, scratch size); -1: CUDA error in *err.
 int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t stream, cudaError_t* err);
 
 // tcgen05 / TMEM GEMM for fp16 activations, M >= 1 (decode, skinny and prefill).

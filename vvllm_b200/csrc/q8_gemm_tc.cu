@@ -493,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float scale = nv ? p.scales[n] : 0.0f;
             const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
             const OT* rrow = (p.res && nv) ? reinterpret_cast<const OT*>(p.res) + (size_t)m0 * p.N + n : nullptr;
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            // one verdict for all four epilogue warps: named barrier 1 follows
+            ok = tc::bar_all<1, 128>(tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
             if (!ok) break;
             tc::tc_fence_after();
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
@@ -543,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     slot++;
                                 }
                         }
-                        ok = __all_sync(0xffffffffu, tc::mbar_wait(redbar, redphase, abort, kWaitTimeoutNs));
+                        ok = tc::bar_all<1, 128>(tc::mbar_wait(redbar, redphase, abort, kWaitTimeoutNs));
                         redphase ^= 1u;
                         if (!ok) {  // let the copies in flight land before the CTA can exit
                             const int zero = 0;

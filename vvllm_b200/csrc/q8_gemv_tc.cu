@@ -249,7 +249,8 @@ __device__ __forceinline__ int token_exp(float m_all, int bad)
 template <typename XT>
 __global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restrict__ x, int K,
                                                           const unsigned long long* wait_counts, int wait_n,
-                                                          unsigned int wait_seq, int pro, const float* norm_w,
+                                                          unsigned int wait_seq, unsigned long long wait_ns,
+                                                          int pro, const float* norm_w,
                                                           float eps, int* __restrict__ part, XT* __restrict__ act_out)
 {
     pdl_launch_dependents();  // the GEMV may start streaming weights right away
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restric
     const int sp = blockIdx.y, ns = gridDim.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // x is the gathered output of a deferred call: every rank's part must have landed
-    if (tid == 0 && wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, kPeerTimeoutNs))
+    if (tid == 0 && wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, wait_ns))
         atomicOr(&g_kernel_error_i8, 2);
     __syncthreads();
     const XT* xrow = x + (size_t)m * (pro == kProSiluMul ? 2 * (size_t)K : (size_t)K);
@@ -546,7 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();  // x (and the prep kernel's exponents) are ready
         // x is the gathered output of the previous call: wait until every rank's part landed
         if (p.po.wait_seq && dtid == 0 &&
-            !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq, kPeerTimeoutNs)) {
+            !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq,
+                              p.po.wait_timeout_ns ? p.po.wait_timeout_ns : kPeerTimeoutNs)) {
             atomicOr(&g_kernel_error_i8, 2);
             raise_error(abort);
         }
@@ -636,8 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool nv = n < p.N;
             const float scale = nv ? p.scales[n] : 0.0f;
             const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
-            ok = __all_sync(0xffffffffu,
-                            tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            // one verdict for all four epilogue warps: named barrier 1 follows
+            ok = tc::bar_all<1, 128>(tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
             if (!ok) break;
             tc::tc_fence_after();
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
@@ -941,7 +943,8 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)ns), dim3(kSqThreads), 0, stream, a.pdl,
                   reinterpret_cast<const XT*>(a.x), (int)a.K, p.po.wait_counts, p.po.wait_n, prep_wait_seq,
-                  a.prologue, a.norm_w, a.eps, sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
+                  p.po.wait_timeout_ns ? p.po.wait_timeout_ns : (unsigned long long)kPeerTimeoutNs, a.prologue,
+                  a.norm_w, a.eps, sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
     if (e != cudaSuccess) return e;
     return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
 }
@@ -965,7 +968,7 @@ int gemv_i8_max_tokens() { return kMaxTokens; }
 bool gemv_i8_fused_exps(const LinearArgs& a)
 {
     // A prologue is applied by the prep kernel, which writes the activations once.
-    if (a.M > (size_t)kFusedExpTokens || a.prologue != kProNone) return false;
+    if (a.M > (size_t)kFusedExpTokens || a.prologue != kProNone || a.force_prep) return false;
     // fp16: the scan (Inf/NaN flags only) is the epilogue warps' alone, off the digits' path
     if (a.in_dtype == kF16 && a.M == 1 && a.K <= kFusedExpMaxKSmall) return true;
     return a.K <= kFusedExpMaxK || (a.N * a.K <= kInKernelScanMaxBytes && a.K <= kFusedExpMaxKSmall);
@@ -1068,7 +1071,8 @@ cudaError_t noalloc_base(int dev, void** out)
 }  // namespace
 
 // Returns 0 and launches, or a reason the shape exceeds the array's limits
-// (1: tokens, 2: rows, 3: SM count, 4: K / alignment), or -1 with *err set.
+// (1: tokens, 2: rows, 3: SM count, 4: K / alignment, 5: scratch beyond the array),
+// or -1 with *err set.
 int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t stream, cudaError_t* err)
 {
     *err = cudaSuccess;
@@ -1083,6 +1087,13 @@ int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t str
         *err = cudaErrorInvalidDevice;
         return -1;
     }
+    // The limits above keep every grid the launch can pick inside the array; check it anyway,
+    // so a shape outside it is refused as such rather than reported as a failed allocation.
+    size_t need_ws = 0, need_ctr = 0, need_act = 0, need_exps = 0;
+    gemv_i8_scratch_need(a, num_sms, &need_ws, &need_ctr, &need_act, &need_exps);
+    if (need_ws > kNoAllocPartialInts || need_ctr > (size_t)kNoAllocMaxTiles || need_exps > kNoAllocExps ||
+        need_act > 0)
+        return 5;
     void* base = nullptr;
     if ((*err = noalloc_base(dev, &base)) != cudaSuccess) return -1;
     TcScratch sc;

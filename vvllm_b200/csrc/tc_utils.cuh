@@ -76,6 +76,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const v
     }
 }
 
+// AND of `ok` over the NT threads of named barrier ID, returned to all of them (also a
+// barrier).  Roles whose threads meet at named barriers later must leave their loops
+// together: a bounded wait decided warp by warp could send one warp out of the loop while
+// another goes on to a barrier the first never reaches.
+template <int ID, int NT>
+__device__ __forceinline__ bool bar_all(bool ok)
+{
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, %3, p; selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "n"(ID), "n"(NT)
+        : "memory");
+    return r != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled load global -> shared, completing on an mbarrier (no multicast).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
