@@ -249,16 +249,17 @@ B200Q8_API int b200q8_silu_mul(void* out, const void* gate_up, int dtype, size_t
 B200Q8_API int b200q8_kernel_error(int* code, int clear);
 
 /* Diagnostics (no vvllm counterpart): the bounded wait a gathered call makes for its peers'
- * completion counts (b200q8_linear_q8_sharded_p2p), run on caller memory so that a failure test
- * can make it run out on one GPU -- a count that nothing advances stands for a rank that never
- * finished.  counts [n] (device uint64, 1 <= n <= 8) must each reach seq * 2^20 (wrapping
- * compare) within timeout_s (0.001 .. 10 s); otherwise bit 1 of b200q8_kernel_error is set and
- * the kernel returns.  where: 0 = the standalone wait kernel (what b200q8_comm_wait enqueues);
- * 1 = inside the int8 digit GEMV before it reads x (how a deferred wait is paid; a give-up also
- * sets bit 0 and the GEMV's outputs are invalid); 2 = inside that GEMV's per-token prep kernel.
- * For 1 and 2 the GEMV out[1, N] = linear_q8(x[1, K], weight[N, K], scales) runs with fp16 x and
- * out, exactly as b200q8_linear_q8_ex(..., B200Q8_ALGO_TC_I8) would. */
-B200Q8_API int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, double timeout_s, int where,
+ * outputs (b200q8_linear_q8_sharded_p2p), run on caller memory so that a failure test can make
+ * it run out on one GPU -- a count that nothing advances stands for a rank that never finished.
+ * counts [n] (device uint64, 1 <= n <= 8) are completion counts as the gathered calls keep them
+ * (2^20 per finished call); the wait holds until every counts[j] holds as many whole calls as
+ * counts[self], within timeout_s (0.001 .. 10 s); otherwise bit 1 of b200q8_kernel_error is set
+ * and the kernel returns.  where: 0 = the standalone wait kernel (what b200q8_comm_wait
+ * enqueues); 1 = inside the int8 digit GEMV before it reads x (how a deferred wait is paid; a
+ * give-up also sets bit 0 and the GEMV's outputs are invalid); 2 = inside that GEMV's per-token
+ * prep kernel.  For 1 and 2 the GEMV out[1, N] = linear_q8(x[1, K], weight[N, K], scales) runs
+ * with fp16 x and out, exactly as b200q8_linear_q8_ex(..., B200Q8_ALGO_TC_I8) would. */
+B200Q8_API int b200q8_diag_peer_wait(const uint64_t* counts, int n, int self, double timeout_s, int where,
                                      void* out, const void* x, const int8_t* weight, const float* scales, size_t N,
                                      size_t K, b200q8_stream_t stream);
 
@@ -340,26 +341,35 @@ B200Q8_API int b200q8_comm_sym_free(b200q8_comm* comm, void* local);
 
 /* Sharded layer with the gather fused into the GEMV: each rank's kernel stores
  * its [M, rows] slice straight into columns [row0, row0 + rows) of `out` on
- * EVERY rank (peer stores over NVLink); every CTA then adds its share of the
- * call's completion count on each rank (system-scope release reduction), and
- * a one-thread wait kernel on `stream` acquires every rank's count (bounded:
- * 2 s, then bit 1 of b200q8_kernel_error).  `out` [M, N] of out_dtype must
+ * EVERY rank (peer stores over NVLink).  A one-thread kernel behind it, once the
+ * GEMV has completed, makes those stores visible system-wide and adds the call
+ * to its completion count on each rank, then acquires every rank's count
+ * (bounded: 2 s, then bit 1 of b200q8_kernel_error).  After a bounded wait gave
+ * up in the int8 GEMV (the error word is set) nothing more is published until
+ * b200q8_kernel_error clears it, so the peers' waits run out as well instead of
+ * reading invalid outputs.  `out` [M, N] of out_dtype must
  * lie inside one b200q8_comm_sym_alloc buffer at the same offset on every
  * rank.  M <= 42; K % 16 == 0 and 16 <= K <= 131072; every rank must own rows.
  * A peer may run one call ahead of this rank, so consecutive calls must use
  * different `out` buffers (double-buffer) unless the caller has finished
  * reading the previous result before the peers can start the next call.
- * The first call allocates the completion counts (collective: all ranks make it). */
+ * Every wait is relative -- each rank waits until every rank has completed as
+ * many gathered calls as itself -- so nothing in a call is tied to the host's
+ * count of calls: a sequence of these calls (with b200q8_comm_wait) may be
+ * captured in a CUDA graph and replayed, the same sequence on every rank.
+ * The first call allocates the completion counts (collective: all ranks make it,
+ * outside any stream capture). */
 B200Q8_API int b200q8_linear_q8_sharded_p2p(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
                                             int in_dtype, const int8_t* w_shard, const float* scales_shard,
                                             const float* bias_shard, size_t M, size_t N, size_t K,
                                             b200q8_stream_t stream);
 
-/* As b200q8_linear_q8_sharded_p2p, with B200Q8_P2P_DEFER_WAIT in `flags`: the call enqueues no
- * wait, so `out` is NOT yet complete in stream order.  The wait is owed by the communicator and
- * paid by its next gathered call (inside the first of that call's kernels that reads its input)
- * or by b200q8_comm_wait.  Any other consumer of `out` must come after b200q8_comm_wait on the
- * same stream.  Chains of deferred calls must stay on one stream. */
+/* As b200q8_linear_q8_sharded_p2p, with B200Q8_P2P_DEFER_WAIT in `flags`: the call publishes
+ * but enqueues no wait, so `out` is NOT yet complete in stream order.  The wait is owed by the
+ * communicator and paid by its next gathered call (inside the first of that call's kernels that
+ * reads its input) or by b200q8_comm_wait.  Any other consumer of `out` must come after
+ * b200q8_comm_wait on the same stream.  Chains of deferred calls must stay on one stream, with
+ * no kernel of their own between them that lets its dependents start before it completes. */
 #define B200Q8_P2P_DEFER_WAIT 1u
 B200Q8_API int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* comm, void* out, int out_dtype, const void* inp,
                                                int in_dtype, const int8_t* w_shard, const float* scales_shard,

@@ -134,9 +134,9 @@ def test_diag_peer_wait_argument_errors():
     L = _lib.lib()
     assert L.b200q8_diag_peer_wait(None, 1, 1, 0.1, 0, None, None, None, None, 0, 0, None) == -1
     assert L.b200q8_diag_peer_wait(1 << 20, 9, 1, 0.1, 0, None, None, None, None, 0, 0, None) == -1
-    assert L.b200q8_diag_peer_wait(1 << 20, 1, 0, 0.1, 0, None, None, None, None, 0, 0, None) == -1
-    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 20.0, 0, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 0.1, 0, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 0, 20.0, 0, None, None, None, None, 0, 0, None) == -1
     assert b"timeout" in L.b200q8_last_error()
-    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 0.1, 3, None, None, None, None, 0, 0, None) == -1
-    assert L.b200q8_diag_peer_wait(1 << 20, 1, 1, 0.1, 1, None, None, None, None, 16, 16, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 0, 0.1, 3, None, None, None, None, 0, 0, None) == -1
+    assert L.b200q8_diag_peer_wait(1 << 20, 1, 0, 0.1, 1, None, None, None, None, 16, 16, None) == -1
     assert b"GEMV needs" in L.b200q8_last_error()

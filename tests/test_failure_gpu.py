@@ -26,7 +26,7 @@ from tests._util import TOL_F16, make_weight, make_x, rowwise_normwise_err
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-SHIFT = 20  # each gathered call adds 2^20 to a rank's completion count
+SHIFT = 20  # each finished gathered call adds 2^20 to a rank's completion count
 
 
 def _inputs(cuda, oracle, N, K, seed):
@@ -42,21 +42,23 @@ def _reference(oracle, q, s, x):
     return oracle.linear_q8(x.astype(np.float32), q, s, None)
 
 
-@pytest.mark.parametrize("n", [1, 8])
+@pytest.mark.parametrize("n", [2, 8])
 def test_standalone_wait_runs_out_and_reports(cuda, n):
     import torch
 
     import vvllm_b200 as v
 
     assert v.kernel_error(clear=True) == 0
-    counts = torch.zeros(n, dtype=torch.int64, device=cuda)  # nothing ever advances these
-    v.diag_peer_wait(counts, seq=1, timeout_s=0.05, where=0)
+    # this rank (the last slot) has finished one call; nothing ever advances the others
+    counts = torch.zeros(n, dtype=torch.int64, device=cuda)
+    counts[n - 1] = 1 << SHIFT
+    v.diag_peer_wait(counts, n - 1, timeout_s=0.05, where=0)
     torch.cuda.synchronize()  # returns: the kernel gave up after 50 ms
     assert v.kernel_error(clear=False) & 2
     v.kernel_error(clear=True)
     assert v.kernel_error(clear=False) == 0
     counts.fill_(1 << SHIFT)  # every rank's call 1 has landed: no error
-    v.diag_peer_wait(counts, seq=1, timeout_s=0.05, where=0)
+    v.diag_peer_wait(counts, n - 1, timeout_s=0.05, where=0)
     torch.cuda.synchronize()
     assert v.kernel_error() == 0
 
@@ -70,8 +72,9 @@ def test_wait_inside_gemv_runs_out_then_recovers(cuda, oracle, where, N, K):
     assert v.kernel_error(clear=True) == 0
     q, s, x, qt, st, xt = _inputs(cuda, oracle, N, K, 1300 + where)
     counts = torch.zeros(2, dtype=torch.int64, device=cuda)
+    counts[0] = 3 << SHIFT  # this rank (slot 0) has finished three calls, its peer none
     out = torch.zeros((1, N), dtype=torch.float16, device=cuda)
-    v.diag_peer_wait(counts, seq=3, timeout_s=0.05, where=where, out=out, x=xt, w=qt, scales=st)
+    v.diag_peer_wait(counts, 0, timeout_s=0.05, where=where, out=out, x=xt, w=qt, scales=st)
     torch.cuda.synchronize()
     code = v.kernel_error(clear=False)
     assert code & 2, code  # the peer wait ran out ...
@@ -87,9 +90,9 @@ def test_wait_inside_gemv_runs_out_then_recovers(cuda, oracle, where, N, K):
     ref = _reference(oracle, q, s, x)
     assert rowwise_normwise_err(y.float().cpu().numpy(), ref) <= TOL_F16
     # the same wait with the counts reached: the GEMV behind it is the ordinary kernel's result
-    counts.fill_(3 << SHIFT)
+    counts[1] = (3 << SHIFT) + 5  # the peer's three calls have landed (and part of a fourth)
     out.zero_()
-    v.diag_peer_wait(counts, seq=3, timeout_s=0.05, where=where, out=out, x=xt, w=qt, scales=st)
+    v.diag_peer_wait(counts, 0, timeout_s=0.05, where=where, out=out, x=xt, w=qt, scales=st)
     torch.cuda.synchronize()
     assert v.kernel_error() == 0
     np.testing.assert_array_equal(out.cpu().numpy(), y.cpu().numpy())

@@ -36,7 +36,7 @@ _SIGS = {
     "b200q8_linear_q8_add": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_linear_q8_ex": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _int, _vp], _int),
     "b200q8_kernel_error": ([ctypes.POINTER(_int), _int], _int),
-    "b200q8_diag_peer_wait": ([_vp, _int, ctypes.c_uint, ctypes.c_double, _int, _vp, _vp, _vp, _vp, _sz, _sz, _vp],
+    "b200q8_diag_peer_wait": ([_vp, _int, _int, ctypes.c_double, _int, _vp, _vp, _vp, _vp, _sz, _sz, _vp],
                               _int),
     "b200q8_linear_q8_noalloc": ([_vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
     "b200q8_backend_create": ([_int, _int, ctypes.POINTER(_vp)], _int),
@@ -336,14 +336,15 @@ def kernel_error(clear: bool = True) -> int:
     return c.value
 
 
-def diag_peer_wait(counts, seq: int, timeout_s: float, where: int = 0, out=None, x=None, w=None, scales=None,
+def diag_peer_wait(counts, self_index: int, timeout_s: float, where: int = 0, out=None, x=None, w=None, scales=None,
                    stream=None) -> None:
-    """The gathered calls' bounded peer wait on `counts` (uint64 / int64 device tensor of n words):
-    where 0 = the standalone wait kernel, 1 = inside the digit GEMV, 2 = inside its prep kernel
-    (1 and 2 run out[1, N] = linear_q8(x[1, K] fp16, w, scales) behind the wait).  A wait that runs
-    out is reported by kernel_error() (bit 1), not by this call."""
+    """The gathered calls' bounded peer wait on `counts` (uint64 / int64 device tensor of n
+    completion counts, 2^20 per finished call): it holds until every count holds as many whole
+    calls as counts[self_index].  where 0 = the standalone wait kernel, 1 = inside the digit GEMV,
+    2 = inside its prep kernel (1 and 2 run out[1, N] = linear_q8(x[1, K] fp16, w, scales) behind
+    the wait).  A wait that runs out is reported by kernel_error() (bit 1), not by this call."""
     N, K = (w.shape[0], w.shape[1]) if w is not None else (0, 0)
-    _check(lib().b200q8_diag_peer_wait(_addr(counts), counts.numel(), seq, float(timeout_s), where, _addr(out),
+    _check(lib().b200q8_diag_peer_wait(_addr(counts), counts.numel(), self_index, float(timeout_s), where, _addr(out),
                                        _addr(x), _addr(w), _addr(scales), N, K, _stream(stream)))
 
 

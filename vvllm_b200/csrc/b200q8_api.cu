@@ -401,12 +401,11 @@ int b200q8_linear_q8_ex(void* out, int out_dtype, const void* inp, int in_dtype,
 int b200q8_kernel_error(int* code, int clear)
 {
     if (!code) return fail(B200Q8_ERR_INVALID, "kernel_error: null code");
-    int c1 = 0, c2 = 0, c3 = 0;
+    int c1 = 0, c2 = 0;
     cudaError_t e = read_kernel_error(&c1, clear != 0);
     if (e == cudaSuccess) e = read_kernel_error_i8(&c2, clear != 0);
-    if (e == cudaSuccess) e = read_kernel_error_p2p(&c3, clear != 0);
     if (e != cudaSuccess) return cuda_fail(e, "kernel_error: read device word");
-    *code = c1 | c2 | c3;
+    *code = c1 | c2;
     if (clear && *code) {
         int dev = 0;
         if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -474,12 +473,12 @@ int b200q8_linear_q8_noalloc(void* out, int out_dtype, const void* inp, int in_d
 
 // The bounded wait of the gathered calls, run on caller memory so that a test can make it run
 // out on one GPU (a count nothing advances) and see the status the host reads afterwards.
-int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, double timeout_s, int where, void* out,
+int b200q8_diag_peer_wait(const uint64_t* counts, int n, int self, double timeout_s, int where, void* out,
                           const void* x, const int8_t* weight, const float* scales, size_t N, size_t K,
                           b200q8_stream_t stream)
 {
-    if (!counts || n < 1 || n > kMaxRanks || seq == 0)
-        return fail(B200Q8_ERR_INVALID, "diag_peer_wait: counts, 1 <= n <= %d and seq > 0 required", kMaxRanks);
+    if (!counts || n < 1 || n > kMaxRanks || self < 0 || self >= n)
+        return fail(B200Q8_ERR_INVALID, "diag_peer_wait: counts, 1 <= n <= %d and 0 <= self < n required", kMaxRanks);
     if (!(timeout_s >= 1e-3 && timeout_s <= 10.0))
         return fail(B200Q8_ERR_INVALID, "diag_peer_wait: timeout_s must lie in [0.001, 10]");
     if (where < 0 || where > 2) return fail(B200Q8_ERR_INVALID, "diag_peer_wait: where must be 0, 1 or 2");
@@ -487,7 +486,12 @@ int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, doubl
     const unsigned long long* cts = reinterpret_cast<const unsigned long long*>(counts);
     cudaError_t e;
     if (where == 0) {
-        e = launch_p2p_wait(cts, n, 0, seq, ns, (cudaStream_t)stream);
+        P2POut wo;
+        wo.rank = self;
+        wo.wait_counts = cts;
+        wo.wait_n = n;
+        wo.wait_timeout_ns = ns;
+        e = launch_p2p_sync(wo, false, true, (cudaStream_t)stream);
         return e == cudaSuccess ? B200Q8_OK : cuda_fail(e, "diag_peer_wait: wait launch");
     }
     if (!out || !x || !weight || !scales || N == 0 || K == 0 || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX)
@@ -499,9 +503,9 @@ int b200q8_diag_peer_wait(const uint64_t* counts, int n, unsigned int seq, doubl
     po.ndst = 1;
     po.dst[0] = out;
     po.ldo = (long long)N;
+    po.rank = self;
     po.wait_counts = cts;
     po.wait_n = n;
-    po.wait_seq = seq;
     po.wait_timeout_ns = ns;
     LinearArgs a;
     a.x = x;
@@ -1018,8 +1022,7 @@ struct b200q8_comm {
     cudaStream_t xstream = nullptr;  // internal stream for handle exchanges
     std::vector<SymAlloc> syms;
     SymAlloc flags;                  // u64 counts[nranks] per rank, advanced by the peers' GEMVs
-    unsigned int seq = 0;            // calls of the in-kernel gather so far (identical on all ranks)
-    unsigned int pending = 0;        // seq of a deferred call whose wait is still owed (0: none)
+    bool pending = false;            // a deferred gathered call's wait is still owed
 };
 
 namespace {
@@ -1299,9 +1302,7 @@ int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, co
     }
     po.ldo = (long long)N;
     po.ocol0 = (int)row0;
-    po.publish = 1;
     po.rank = c->rank;
-    po.seq = ++c->seq;
     DeviceInfo d;
     if ((st = device_info(&d))) return st;
     LinearArgs a;
@@ -1329,18 +1330,17 @@ int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, co
     if (c->pending) {
         po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
         po.wait_n = G;
-        po.wait_seq = c->pending;
-        c->pending = 0;
     }
     if ((e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream)) != cudaSuccess)
         return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");
-    if (flags & B200Q8_P2P_DEFER_WAIT) {
-        c->pending = po.seq;  // the next gathered call (or b200q8_comm_wait) waits for it
-        return B200Q8_OK;
-    }
-    if ((e = launch_p2p_wait(reinterpret_cast<const unsigned long long*>(c->flags.local), G, c->rank, po.seq,
-                             2000000000ull, (cudaStream_t)stream)) != cudaSuccess)
-        return cuda_fail(e, "linear_q8_sharded_p2p: wait launch");
+    // Behind the GEMV: publish this call once its grid has completed, and -- unless the wait is
+    // deferred to the next gathered call or b200q8_comm_wait -- wait for every rank's part.
+    const bool defer = (flags & B200Q8_P2P_DEFER_WAIT) != 0;
+    po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
+    po.wait_n = G;
+    if ((e = launch_p2p_sync(po, true, !defer, (cudaStream_t)stream)) != cudaSuccess)
+        return cuda_fail(e, "linear_q8_sharded_p2p: completion launch");
+    c->pending = defer;  // the next gathered call (or b200q8_comm_wait) waits for it
     return B200Q8_OK;
 }
 
@@ -1358,10 +1358,13 @@ int b200q8_comm_wait(b200q8_comm* c, b200q8_stream_t stream)
     if (!c->pending) return B200Q8_OK;
     int st = set_device(c->device);
     if (st) return st;
-    cudaError_t e = launch_p2p_wait(reinterpret_cast<const unsigned long long*>(c->flags.local), c->nranks, c->rank,
-                                    c->pending, 2000000000ull, (cudaStream_t)stream);
+    P2POut po;
+    po.rank = c->rank;
+    po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
+    po.wait_n = c->nranks;
+    cudaError_t e = launch_p2p_sync(po, false, true, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "comm_wait: wait launch");
-    c->pending = 0;
+    c->pending = false;
     return B200Q8_OK;
 }
 

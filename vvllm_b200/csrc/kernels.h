@@ -12,10 +12,20 @@ enum DType : int { kF32 = 0, kF16 = 1 };
 // Output placement for the column-sharded path with an in-kernel gather: every
 // output element is stored into `ndst` copies of the full [M, ldo] output
 // (the local one and each peer's, mapped over NVLink), at column ocol0 + row.
-// Completion: when a CTA is done it adds its share of 2^20 to counts[rank] on
-// every rank (system-scope release reduction; CTA 0 adds 2^20 - (grid - 1), the
-// others 1), so counts[j] on a rank reaches seq * 2^20 once all of rank j's CTAs of
-// call `seq` have stored their outputs there.
+//
+// Completion: the GEMV's CTAs store and retire; they do not wait for the NVLink
+// acknowledgements of their stores.  The small kernel launched behind the GEMV
+// (launch_p2p_sync) passes griddepcontrol.wait once the GEMV grid has completed,
+// then one thread makes its stores visible system-wide (one fence) and adds 2^20
+// to counts[rank] on every rank.  So counts[j] on a rank holds 2^20 per call of
+// rank j whose outputs have landed there.  Nothing is published after a launch
+// that set the device error word (a bounded wait gave up): its peers' waits run
+// out too, instead of reading invalid outputs.
+//
+// Waits are relative, so nothing about them is fixed at launch time and the calls
+// can be captured in a CUDA graph and replayed: after the previous kernel in the
+// stream (the previous call's sync kernel) has completed, a rank's own count holds
+// all of its earlier calls; the wait holds until every counts[j] holds as many.
 constexpr int kMaxRanks = 8;
 constexpr int kCountShift = 20;  // each call adds 2^20 to every rank's count slot
 struct P2POut {
@@ -23,16 +33,13 @@ struct P2POut {
     void* dst[kMaxRanks] = {};
     long long ldo = 0;
     int ocol0 = 0;
-    int publish = 0;                             // add this launch's completion shares
     unsigned long long* counts[kMaxRanks] = {};  // count array base on every rank
     int rank = 0;
-    unsigned int seq = 0;
     // Deferred wait of the previous gathered call: before x (or a residual) is read, every
-    // rank's count in wait_counts[0..wait_n) must have reached wait_seq << kCountShift
-    // (wait_seq 0: nothing to wait for).
+    // rank's count in wait_counts[0..wait_n) must hold as many whole calls as
+    // wait_counts[rank] (this rank's own count).  wait_counts null: nothing to wait for.
     const unsigned long long* wait_counts = nullptr;
     int wait_n = 0;
-    unsigned int wait_seq = 0;
     unsigned long long wait_timeout_ns = 0;  // limit of that wait (0: the default, 2 s)
 };
 
@@ -64,11 +71,13 @@ struct LinearArgs {
     bool force_prep = false;
 };
 
-// One thread waits (bounded, `timeout_ns`) until counts[j] has reached seq << kCountShift for
-// every rank j; on expiry it sets bit 1 of the device error word and returns.
-cudaError_t launch_p2p_wait(const unsigned long long* counts, int nranks, int rank, unsigned int seq,
-                            unsigned long long timeout_ns, cudaStream_t stream);
-cudaError_t read_kernel_error_p2p(int* code, bool clear);
+// The kernel behind a gathered call's GEMV (one thread does the work; it lets its own dependents
+// launch at once, and they pass griddepcontrol.wait only when it is done).  After the previous
+// kernel in the stream has completed: with `publish`, unless the device error word of the digit
+// GEMV is set, one system-scope fence and 2^20 added to counts[d][rank] on each of the ndst
+// ranks; with `wait`, a bounded wait (timeout_ns) until every wait_counts[j], j < n, holds as
+// many whole calls as wait_counts[rank] (bit 1 of the error word on expiry).
+cudaError_t launch_p2p_sync(const P2POut& po, bool publish, bool wait, cudaStream_t stream);
 
 // Streaming SIMT GEMV, M <= gemv_max_tokens().  Also takes any M/K through a
 // generic (slow, correct) kernel when the fast one cannot (alignment, K % 16).

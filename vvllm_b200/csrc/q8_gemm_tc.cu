@@ -62,6 +62,21 @@ namespace b200q8 {
 
 __device__ int g_kernel_error;  // bit 0: a bounded wait timed out in the tensor-core GEMM
 
+// Per-CTA phase timestamps, compiled in only with -DB200Q8_TRACE (a profiling build; the
+// product build has none): [cta][slot] = %globaltimer at slot 0, SM cycles since slot 0 after.
+#ifdef B200Q8_TRACE
+__device__ unsigned long long g_gemm_trace[1024][8];
+#define GEMM_TRACE(slot, t0)                                                                     \
+    do {                                                                                         \
+        if (blockIdx.x < 1024)                                                                   \
+            g_gemm_trace[blockIdx.x][slot] = (slot) == 0 ? tc::globaltimer_ns() : clock64() - (t0); \
+    } while (0)
+#else
+#define GEMM_TRACE(slot, t0) \
+    do {                     \
+    } while (0)
+#endif
+
 namespace {
 
 constexpr int kTileRows = 128;  // weight rows per tile (UMMA M)
@@ -224,7 +239,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sw_base = tc::smem_u32(sW8), sx_base = tc::smem_u32(sX), sout_base = tc::smem_u32(sOut);
 
     int pre = 0;  // stages whose weight boxes were requested before the dependency wait
+    const long long trace_t0 = clock64();
+    (void)trace_t0;
     if (threadIdx.x == 0) {
+        GEMM_TRACE(0, trace_t0);
         for (int s = 0; s < S; s++) {
             tc::mbar_init(full0 + 8u * s, 1);
             tc::mbar_init(empty0 + 8u * s, 1);
@@ -261,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Activations come from the previous kernel; hold no TMEM while waiting for it.
     pdl_wait();
+    if (threadIdx.x == 0) GEMM_TRACE(1, trace_t0);
     __syncwarp();
     if (warp == 1) {
         tc::tmem_alloc(tc::smem_u32(tmem_holder), C::kTmemCols);
@@ -270,6 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    if (threadIdx.x == 0) GEMM_TRACE(2, trace_t0);
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -340,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc::tc_fence_after();
+                    if (seg == 0 && kb == k0) GEMM_TRACE(3, trace_t0);
                     const uint32_t a_base = tmem + C::kACol + sa.idx * C::kACols;
                     // descriptor start address advances in 16-byte units
                     const uint64_t b_stage = bdesc0 + (uint64_t)((st.idx * C::kXBytes) >> 4);
@@ -355,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 tc::mma_commit(accfull0 + 8u * ab);
+                GEMM_TRACE(4, trace_t0);
                 seg++;
             }
             if (*abort) {
@@ -496,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // one verdict for all four epilogue warps: named barrier 1 follows
             ok = tc::bar_all<1, 128>(tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
             if (!ok) break;
+            if (etid == 0 && seg == 0) GEMM_TRACE(5, trace_t0);
             tc::tc_fence_after();
             const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
             const long long tb = (long long)t * p.kbpt;
@@ -639,6 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) raise_error(abort);
         if (etid == 0) tc::bulk_wait_all();  // outputs written before the dependents may look
+        if (etid == 0) GEMM_TRACE(6, trace_t0);
         pdl_launch_dependents();
     }
 
@@ -650,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, C::kTmemCols);
     }
+    if (threadIdx.x == 0) GEMM_TRACE(7, trace_t0);
 }
 
 // ----------------------------------------------------------------------------- host
@@ -826,6 +851,15 @@ cudaError_t launch_q8_gemm_tc(const LinearArgs& a, int num_sms, const TcScratch&
     return a.out_dtype == kF16 ? launch_typed<__half>(a, num_sms, scratch, stream)
                                : launch_typed<float>(a, num_sms, scratch, stream);
 }
+
+#ifdef B200Q8_TRACE
+// Profiling build only: copies the per-CTA phase timestamps of the last GEMM launches.
+extern "C" __attribute__((visibility("default"))) int b200q8_trace_gemm(void* dst, size_t bytes)
+{
+    if (bytes > sizeof(g_gemm_trace)) bytes = sizeof(g_gemm_trace);
+    return cudaMemcpyFromSymbol(dst, g_gemm_trace, bytes) == cudaSuccess ? 0 : -2;
+}
+#endif
 
 cudaError_t read_kernel_error(int* code, bool clear)
 {

@@ -48,6 +48,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "p2p.cuh"
 #include "prologue.cuh"
 #include "sk_common.cuh"
 #include "tc_utils.cuh"
@@ -126,24 +127,6 @@ __device__ __forceinline__ void raise_error(volatile int* abort)
 {
     *abort = 1;
     atomicOr(&g_kernel_error_i8, 1);
-}
-
-// Bounded wait until counts[j] has reached seq << kCountShift (wrapping compare) for every
-// j < n, each read with system-scope acquire; false after timeout_ns.
-__device__ bool wait_peer_counts(const unsigned long long* counts, int n, unsigned int seq, uint64_t timeout_ns)
-{
-    const unsigned long long target = (unsigned long long)seq << kCountShift;
-    const uint64_t t0 = tc::globaltimer_ns();
-    for (int j = 0; j < n; j++) {
-        for (;;) {
-            unsigned long long v;
-            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counts + j) : "memory");
-            if ((long long)(v - target) >= 0) break;
-            if (tc::globaltimer_ns() - t0 > timeout_ns) return false;
-            __nanosleep(32);
-        }
-    }
-    return true;
 }
 
 // Bounded wait until a split tile's arrival counter reaches `target` (read with gpu-scope
@@ -249,7 +232,7 @@ __device__ __forceinline__ int token_exp(float m_all, int bad)
 template <typename XT>
 __global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restrict__ x, int K,
                                                           const unsigned long long* wait_counts, int wait_n,
-                                                          unsigned int wait_seq, unsigned long long wait_ns,
+                                                          int wait_self, unsigned long long wait_ns,
                                                           int pro, const float* norm_w,
                                                           float eps, int* __restrict__ part, XT* __restrict__ act_out)
 {
@@ -262,7 +245,7 @@ __global__ void __launch_bounds__(kSqThreads, 6) exps_kernel(const XT* __restric
     const int sp = blockIdx.y, ns = gridDim.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // x is the gathered output of a deferred call: every rank's part must have landed
-    if (tid == 0 && wait_seq && !wait_peer_counts(wait_counts, wait_n, wait_seq, wait_ns))
+    if (tid == 0 && wait_counts && !wait_peers(wait_counts, wait_n, wait_self, wait_ns))
         atomicOr(&g_kernel_error_i8, 2);
     __syncthreads();
     const XT* xrow = x + (size_t)m * (pro == kProSiluMul ? 2 * (size_t)K : (size_t)K);
@@ -546,13 +529,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int dtid = threadIdx.x - kFirstDig * 32;  // 0..127
         pdl_wait();  // x (and the prep kernel's exponents) are ready
         // x is the gathered output of the previous call: wait until every rank's part landed
-        if (p.po.wait_seq && dtid == 0 &&
-            !wait_peer_counts(p.po.wait_counts, p.po.wait_n, p.po.wait_seq,
-                              p.po.wait_timeout_ns ? p.po.wait_timeout_ns : kPeerTimeoutNs)) {
+        if (p.po.wait_counts && dtid == 0 &&
+            !wait_peers(p.po.wait_counts, p.po.wait_n, p.po.rank,
+                        p.po.wait_timeout_ns ? p.po.wait_timeout_ns : kPeerTimeoutNs)) {
             atomicOr(&g_kernel_error_i8, 2);
             raise_error(abort);
         }
-        if (p.po.wait_seq)
+        if (p.po.wait_counts)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed (the epilogue reads them too)
         // fp32: the per-token exponents into shared memory, by the epilogue and digitizer warps
         // together (found here for few tokens, else folded from the prep kernel's words).  fp16
@@ -568,26 +551,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         sk::SegIter it(u_begin, u_end, p.kbpt);
         bool ok = true;
         const XT* xg = reinterpret_cast<const XT*>(p.x);
+        // Thread -> items of 4 consecutive k of one token (BK/4 items per token per stage), at most
+        // kItems per thread.  Every load of a stage is issued first, before the wait for the ring
+        // slot: one L2 round trip per stage, overlapping the wait, instead of one per item.
+        constexpr int kItems = ((NC / kDigits) * (BK / 4) + 127) / 128;
+        const int nitems = p.M * (BK / 4);
         while (ok && it.next(t, k0, k1)) {
             for (int kb = k0; kb < k1; kb++, g++, st.next(S)) {
+                float v[kItems][4];
+#pragma unroll
+                for (int j = 0; j < kItems; j++) {
+                    const int item = dtid + j * 128;
+                    const int m = item / (BK / 4);
+                    const int k = kb * BK + (item - m * (BK / 4)) * 4;
+                    if (item < nitems && k < p.K) {
+                        load4<XT>(xg + (size_t)m * p.K + k, v[j]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[j][i] = 0.0f;
+                    }
+                }
                 if (g >= S) {
                     ok = __all_sync(0xffffffffu,
                                     tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs));
                     if (!ok) break;
                 }
                 unsigned char* bst = sD + st.idx * C::kDBytes;
-                // thread -> 4 consecutive k of one token; BK/4 groups per token per stage
-                for (int item = dtid; item < p.M * (BK / 4); item += 128) {
+#pragma unroll
+                for (int j = 0; j < kItems; j++) {
+                    const int item = dtid + j * 128;
+                    if (item >= nitems) break;
                     const int m = item / (BK / 4);
                     const int kk = (item - m * (BK / 4)) * 4;  // 0..BK-4
-                    const int k = kb * BK + kk;
                     const int e = sizeof(XT) == 2 ? kF16Exp : exps[m];
                     uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
-                    if (k < p.K && e != INT_MIN) {
-                        float v[4];
-                        load4<XT>(xg + (size_t)m * p.K + k, v);
+                    if (e != INT_MIN) {  // beyond K the values are 0: zero digits
 #pragma unroll
-                        for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
+                        for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[j][i], e)), d, i);
                     }
                     const int h = kk >> 7, c = (kk & 127) >> 4, byte = kk & 15;
 #pragma unroll
@@ -611,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (threadIdx.x - kFirstEpi * 32 < p.M) s_best[threadIdx.x - kFirstEpi * 32] = 0ull;
             asm volatile("bar.sync 1, 128;" ::: "memory");
         }
-        if (p.po.wait_seq)
+        if (p.po.wait_counts)
             asm volatile("bar.sync 3, 256;" ::: "memory");  // peers' outputs landed
         // the per-token exponents, once per CTA (read for every output): fp32 with the digitizer
         // warps; fp16 (only the Inf/NaN flags) by these warps alone while the digits stream
@@ -796,19 +796,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             *p.amax_done = 0;
         }
     }
-    if (p.po.publish && threadIdx.x == 0 && !*abort) {
-        // This CTA's output stores (every thread's, ordered before this point by the barrier
-        // above) are released to every rank together with its share of the call's count; the
-        // shares of the grid sum to 2^kCountShift.  This rank's own count last.  A CTA that
-        // gave up on a bounded wait publishes nothing, so its call never completes anywhere.
-        const unsigned long long share =
-            blockIdx.x == 0 ? (1ull << kCountShift) - (unsigned long long)(gridDim.x - 1) : 1ull;
-        for (int i = 1; i <= p.po.ndst; i++) {
-            const int d = (p.po.rank + i) % p.po.ndst;
-            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p.po.counts[d] + p.po.rank), "l"(share)
-                         : "memory");
-        }
+}
+
+// Completion of a gathered call (kernels.h, P2POut), launched behind its GEMV.  One thread:
+// after the GEMV grid has completed (griddepcontrol.wait: its stores are performed), publish
+// this call -- unless a bounded wait gave up somewhere in the digit GEMV, whose outputs are then
+// invalid -- and/or wait for every rank's outputs of the calls so far.
+__global__ void p2p_sync_kernel(const P2POut po, int publish, int wait)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    if (publish) {
+        int err;
+        asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(err) : "l"(&g_kernel_error_i8) : "memory");
+        if (err == 0) publish_share(po.counts, po.ndst, po.rank, 1ull << kCountShift);
     }
+    if (wait && !wait_peers(po.wait_counts, po.wait_n, po.rank,
+                            po.wait_timeout_ns ? po.wait_timeout_ns : kPeerTimeoutNs))
+        atomicOr(&g_kernel_error_i8, 2);
 }
 
 // ----------------------------------------------------------------------------- host
@@ -930,8 +936,8 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         p.po.ocol0 = 0;
     }
     // Without in-kernel exponents the prep kernel reads x first: it pays the deferred wait.
-    const unsigned int prep_wait_seq = p.fused_exps ? 0u : p.po.wait_seq;
-    if (!p.fused_exps) p.po.wait_seq = 0;
+    const unsigned long long* prep_wait = p.fused_exps ? nullptr : p.po.wait_counts;
+    if (!p.fused_exps) p.po.wait_counts = nullptr;
     const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
     // A prologue: the prep kernel writes the activations once, the GEMV reads them as plain x.
     const bool materialize = a.prologue != kProNone;
@@ -942,7 +948,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)ns), dim3(kSqThreads), 0, stream, a.pdl,
-                  reinterpret_cast<const XT*>(a.x), (int)a.K, p.po.wait_counts, p.po.wait_n, prep_wait_seq,
+                  reinterpret_cast<const XT*>(a.x), (int)a.K, prep_wait, p.po.wait_n, p.po.rank,
                   p.po.wait_timeout_ns ? p.po.wait_timeout_ns : (unsigned long long)kPeerTimeoutNs, a.prologue,
                   a.norm_w, a.eps, sc.exps, materialize ? reinterpret_cast<XT*>(sc.act) : nullptr);
     if (e != cudaSuccess) return e;
@@ -1004,6 +1010,12 @@ cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch&
                                    : launch_typed<__half, float>(a, num_sms, sc, stream);
     return a.out_dtype == kF16 ? launch_typed<float, __half>(a, num_sms, sc, stream)
                                : launch_typed<float, float>(a, num_sms, sc, stream);
+}
+
+cudaError_t launch_p2p_sync(const P2POut& po, bool publish, bool wait, cudaStream_t stream)
+{
+    if (wait && !po.wait_counts) return cudaErrorInvalidValue;
+    return launch_ex(p2p_sync_kernel, dim3(1), dim3(32), 0, stream, true, po, publish ? 1 : 0, wait ? 1 : 0);
 }
 
 cudaError_t read_kernel_error_i8(int* code, bool clear)
