@@ -254,6 +254,7 @@ def run_reference(args):
     sample = (f"{frac:.3f} of the rows of each projection ({sample_bytes / 1e6:.1f} MB algorithmic per step, "
               f"> 2x the host's {llc_bytes() / 2**20:.0f} MiB LLC), fp32 activations widened from fp16, "
               f"{cores} threads on disjoint output-channel slices; CPU: {model}")
+    ref_gpu = reference_gpu(args)
     line = {
         "metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -264,8 +265,79 @@ def run_reference(args):
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_gpu(args):
+    """The reference's own GPU linear_q8 (vvllm::BackendCUDA, fp16 mode: cuBLAS GemmEx on the fp16
+    dequantized copy of each int8 weight, src/backend/backend_cuda.cc:188-213), built from the
+    reference sources for sm_100a into oracle/_ref/libvvllm_refgpu.so, on the same 7B decode step
+    (gate_up, down, lm_head, one fp16 token) on GPU 0; None without a GPU or that library.  Timed
+    with CUDA events on the legacy default stream the reference launches on, over the K steps
+    after W warm-up steps (the first call of each weight uploads and dequantizes it).  `value`
+    uses this bench's algorithmic bytes (int8 weights), so it compares with the B200 arm's value
+    directly; `fp16_weight_gbs` counts the 2 bytes per weight cuBLAS actually streams."""
+    import ctypes
+
+    path = os.path.join(ROOT, "oracle", "_ref", "libvvllm_refgpu.so")
+    try:
+        import torch
+
+        if not torch.cuda.is_available() or not os.path.exists(path):
+            return None
+    except ImportError:
+        return None
+    import vvllm_b200
+
+    vvllm_b200.lib()  # the reference GPU library links the in-tree libb200q8.so (its adapter)
+    L = ctypes.CDLL(path)
+    L.vref_gpu_create.restype = ctypes.c_void_p
+    L.vref_gpu_create.argtypes = [ctypes.c_int]
+    L.vref_gpu_linear_q8.restype = ctypes.c_int
+    L.vref_gpu_linear_q8.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_size_t] * 3
+    L.vref_gpu_destroy.argtypes = [ctypes.c_void_p]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(9)
+    block = rng.integers(-127, 128, size=1 << 23, dtype=np.int8)
+    host = []
+    for name, N, K in PROJ:
+        q = np.resize(block, N * K).reshape(N, K)
+        s = (rng.random(N, dtype=np.float32) * np.float32(1e-3)).astype(np.float32)
+        x = torch.randn(1, K, device=dev).half()
+        out = torch.empty(1, N, device=dev, dtype=torch.float16)
+        host.append((q, s, x, out, N, K))
+    be = L.vref_gpu_create(1)
+    stream = torch.cuda.default_stream(dev)
+
+    def step():
+        for q, s, x, out, N, K in host:
+            if L.vref_gpu_linear_q8(be, out.data_ptr(), x.data_ptr(), q.ctypes.data, s.ctypes.data, None, 1, N, K):
+                raise RuntimeError("reference BackendCUDA::linear_q8 failed")
+
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.steps):
+                step()
+            b.record(stream)
+            torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+    finally:
+        L.vref_gpu_destroy(be)
+    nb = sum(algo_bytes(N, K) for _, N, K in PROJ)
+    nb16 = sum(2 * N * K + 2 * K + 2 * N for _, N, K in PROJ)
+    return {"value": round(nb / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
+            "fp16_weight_gbs": round(nb16 / (ms * 1e-3) / 1e9, 2), "steps": args.steps,
+            "path": "vvllm::BackendCUDA::linear_q8, fp16 mode (cuBLAS GemmEx on fp16 dequantized weights), "
+                    "reference sources built for sm_100a, one GPU, direct calls on the legacy default stream"}
 
 
 def cpu_quantize(lib, min_bytes: int, budget_s: float):
