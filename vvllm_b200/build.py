@@ -22,7 +22,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200q8.so")
 
 SOURCES = ["b200q8_api.cu", "q8_gemv.cu", "q8_quantize.cu", "q8_gemm_tc.cu", "q8_gemv_tc.cu", "gather.cu", "prologue.cu", "q8st.cu"]
-HEADERS = ["common.cuh", "kernels.h", "tc_utils.cuh", "sk_common.cuh", "tmap.cuh", "prologue.cuh"]
+HEADERS = ["common.cuh", "kernels.h", "tc_utils.cuh", "sk_common.cuh", "tmap.cuh", "prologue.cuh", "p2p.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # No --use_fast_math / -ftz: the quantize kernel must keep denormals and IEEE division.

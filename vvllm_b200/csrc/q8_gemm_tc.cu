@@ -50,6 +50,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -290,6 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     if (threadIdx.x == 0) GEMM_TRACE(2, trace_t0);
+    // The next kernel may be scheduled now: its CTAs take SMs this grid leaves idle and run their
+    // set-up and weight loads; everything they do with this grid's outputs waits in their
+    // griddepcontrol.wait, which returns only once this grid has completed.
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -661,9 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             seg++;
         }
         if (!ok) raise_error(abort);
-        if (etid == 0) tc::bulk_wait_all();  // outputs written before the dependents may look
+        if (etid == 0) tc::bulk_wait_all();  // outputs written before the grid completes
         if (etid == 0) GEMM_TRACE(6, trace_t0);
-        pdl_launch_dependents();
     }
 
     // ---------------------------------------------------------------- teardown
@@ -726,6 +730,9 @@ bool make_out_map(const LinearArgs& a, int CH, CUtensorMap* mo)
 // fixup of the many pieces per tile would cost more than it saves.
 int pick_bn(size_t M, size_t N, int num_sms)
 {
+#ifdef B200Q8_TRACE
+    if (const char* f = getenv("B200Q8_TRACE_BN")) return atoi(f);  // profiling build: forced tile width
+#endif
     if (M <= 16) return 16;
     if (M <= 32) return 32;
     if (M <= 64) return 64;
@@ -746,6 +753,12 @@ int pick_bk(int BN) { return BN <= 32 ? 256 : BN <= 128 ? 128 : 64; }
 long long pick_grid(long long tiles, long long kbpt, int BN, int BK, int num_sms)
 {
     const long long units = tiles * kbpt;
+#ifdef B200Q8_TRACE
+    if (const char* f = getenv("B200Q8_TRACE_GRID")) {  // profiling build: 1 = whole tiles, 2 = stream-K
+        if (atoi(f) == 1) return tiles;
+        if (atoi(f) == 2) return units < num_sms ? units : num_sms;
+    }
+#endif
     const long long sk = units < num_sms ? units : num_sms;
     if (tiles > num_sms || units % sk == 0 && (units / sk) % kbpt == 0) return sk;  // no split anyway
     // per-unit time: BK/16 MMAs of max(issue ~70, BN/2) cycles, at ~1.9 GHz, x1.3 for data movement
@@ -854,8 +867,14 @@ cudaError_t launch_q8_gemm_tc(const LinearArgs& a, int num_sms, const TcScratch&
 
 #ifdef B200Q8_TRACE
 // Profiling build only: copies the per-CTA phase timestamps of the last GEMM launches.
+// dst null: clear them.
 extern "C" __attribute__((visibility("default"))) int b200q8_trace_gemm(void* dst, size_t bytes)
 {
+    if (!dst) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemm_trace) != cudaSuccess) return -2;
+        return cudaMemset(p, 0, sizeof(g_gemm_trace)) == cudaSuccess ? 0 : -2;
+    }
     if (bytes > sizeof(g_gemm_trace)) bytes = sizeof(g_gemm_trace);
     return cudaMemcpyFromSymbol(dst, g_gemm_trace, bytes) == cudaSuccess ? 0 : -2;
 }
