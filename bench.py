@@ -798,7 +798,7 @@ def main():
             q, s = sets[0][i]
             loc = torch.empty((1, per[i] * world), dtype=torch.float16, device=dev)
             mine = loc[:, rank * per[i]:rank * per[i] + per[i]]
-            v.linear_q8_ex(mine[:, :rows], xs[i], q, s, algo=v.ALGO_TC_I8, stream=stream)
+            v.linear_q8(mine[:, :rows], xs[i], q, s, stream=stream)
             full = torch.empty((1, per[i] * world), dtype=torch.float16, device=dev)
             dist.all_gather_into_tensor(full, mine.contiguous())
             same &= int(torch.equal(full[:, :N], p2p_outs[i]))
@@ -806,8 +806,9 @@ def main():
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         parity = {"ok": bool(flag.item()), "ranks": world,
                   "check": "every rank's gathered [1, N] outputs of the last timed step equal, bit for bit, "
-                           "each rank's rows computed by the unsharded digit GEMV (ALGO_TC_I8) and all-gathered "
-                           "by NCCL; the digit GEMV itself is checked against the reference in tests/"}
+                           "each rank's rows computed by the local dispatch (the kernel the gathered call runs "
+                           "per shard) and all-gathered by NCCL; those kernels are checked against the "
+                           "reference in tests/"}
     if world > 1:
         t = torch.tensor([ms, lm_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -339,7 +339,9 @@ B200Q8_API int b200q8_linear_q8_sharded(b200q8_comm* comm, void* out, int out_dt
 B200Q8_API int b200q8_comm_sym_alloc(b200q8_comm* comm, size_t bytes, void** local);
 B200Q8_API int b200q8_comm_sym_free(b200q8_comm* comm, void* local);
 
-/* Sharded layer with the gather fused into the GEMV: each rank's kernel stores
+/* Sharded layer with the gather fused into the GEMV -- the kernel the local dispatch picks for
+ * the shard (b200q8_linear_q8: the streaming GEMV for up to 4 tokens on up to 48 MiB of weights,
+ * else the int8 tensor-core GEMV): each rank's kernel stores
  * its [M, rows] slice straight into columns [row0, row0 + rows) of `out` on
  * EVERY rank (peer stores over NVLink).  A one-thread kernel behind it, once the
  * GEMV has completed, makes those stores visible system-wide and adds the call

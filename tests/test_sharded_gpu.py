@@ -1,11 +1,11 @@
 """Column-sharded linear_q8 over 2, 4 and 8 GPUs (each world size runs where that many GPUs exist).
 
-Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range), runs
-b200q8_linear_q8_sharded, and must end with the full [M, N] output.  Checked
-against the unsharded single-GPU result on the same int8 digit GEMV (it sums exact integers, so
-sharding cannot change its result; the AUTO dispatch would pick the SIMT GEMV for the small
-unsharded shapes, whose float sums differ in the last bit) and against the CPU oracle on a row
-sample.
+Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range) and must end with the
+full [M, N] output, gathered by NCCL (b200q8_linear_q8_sharded) or by the GEMV's own stores into
+every rank's buffer (b200q8_linear_q8_sharded_p2p).  The gathered outputs must equal, bit for
+bit, each shard computed on one GPU by the local dispatch (b200q8_linear_q8 on the shard's rows:
+the kernel the gathered call runs per shard, so the same sums in the same order), and the CPU
+oracle on a row sample within the fp16 tolerance.
 """
 import os
 import socket
@@ -40,6 +40,21 @@ def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _sharded_ref(v, torch, dev, q, s, x, N, world, odt):
+    """Every shard's rows computed on this GPU by the local dispatch, assembled into [M, N]."""
+    M = x.shape[0]
+    out = torch.empty((M, N), dtype=odt, device=dev)
+    qd, sd = torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev)
+    for r in range(world):
+        r0, rows = v.shard_range(N, world, r)
+        if rows == 0:
+            continue
+        part = torch.empty((M, rows), dtype=odt, device=dev)
+        v.linear_q8(part, x, qd[r0:r0 + rows], sd[r0:r0 + rows])
+        out[:, r0:r0 + rows] = part
+    return out
 
 
 def _worker(rank, world, port, path):
@@ -89,12 +104,9 @@ def _worker(rank, world, port, path):
             del bufs
             comm.sym_free(sym)
             del sym
-        if rank == 0:  # the unsharded result on one GPU, on the digit GEMV the fused gather runs per shard
-            full = torch.empty((M, N), dtype=torch.float16, device=dev)
-            v.linear_q8_ex(full, xt, torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev), algo=v.ALGO_TC_I8)
-            fullf = torch.empty((M, N), dtype=torch.float32, device=dev)
-            v.linear_q8_ex(fullf, xt.float(), torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev),
-                           algo=v.ALGO_TC_I8)
+        if rank == 0:  # every shard on one GPU, on the kernel the gathered call runs per shard
+            full = _sharded_ref(v, torch, dev, q, s, xt, N, world, torch.float16)
+            fullf = _sharded_ref(v, torch, dev, q, s, xt.float(), N, world, torch.float32)
             torch.cuda.synchronize()
             results[f"full{ci}"] = full.float().cpu().numpy()
             results[f"fullf{ci}"] = fullf.cpu().numpy()
@@ -121,12 +133,8 @@ def _worker(rank, world, port, path):
         torch.cuda.synchronize()
         results[f"chain{ci}"] = y2.float().cpu().numpy()
         if rank == 0:
-            f1 = torch.empty((M, N1), dtype=torch.float16, device=dev)
-            f2 = torch.empty((M, N2), dtype=torch.float16, device=dev)
-            v.linear_q8_ex(f1, x, torch.from_numpy(data["q1"]).to(dev), torch.from_numpy(data["s1"]).to(dev),
-                           algo=v.ALGO_TC_I8)
-            v.linear_q8_ex(f2, f1, torch.from_numpy(data["q2"]).to(dev), torch.from_numpy(data["s2"]).to(dev),
-                           algo=v.ALGO_TC_I8)
+            f1 = _sharded_ref(v, torch, dev, data["q1"], data["s1"], x, N1, world, torch.float16)
+            f2 = _sharded_ref(v, torch, dev, data["q2"], data["s2"], f1, N2, world, torch.float16)
             torch.cuda.synchronize()
             results[f"chainref{ci}"] = f2.float().cpu().numpy()
         del y1, y2
@@ -163,7 +171,7 @@ def test_sharded(tmp_path, oracle, world):
         for i in range(world):
             got = r[i][f"out{ci}"]
             assert rowwise_normwise_err(got, full) <= TOL_F16, (ci, i)
-            # The fused gather runs the same integer-exact kernel per shard: bit-identical.
+            # The fused gather runs the local dispatch's kernel per shard: bit-identical.
             for b in (0, 1):
                 np.testing.assert_array_equal(r[i][f"p2ph{ci}_{b}"], full, err_msg=f"case {ci} rank {i} buf {b}")
                 np.testing.assert_array_equal(r[i][f"p2pf{ci}_{b}"], r[0][f"fullf{ci}"],
@@ -173,5 +181,5 @@ def test_sharded(tmp_path, oracle, world):
         ref = oracle.linear_q8(data["x"], data["q"][rows], data["s"][rows], None)
         assert rowwise_normwise_err(r[1][f"out{ci}"][:, rows], ref) <= TOL_F16, ci
     for ci in range(len(CHAIN)):
-        for i in range(world):  # deferred-wait chain: bit-identical to the single-GPU chain
+        for i in range(world):  # deferred-wait chain: bit-identical to the shards computed on one GPU
             np.testing.assert_array_equal(r[i][f"chain{ci}"], r[0][f"chainref{ci}"], err_msg=f"chain {ci} rank {i}")

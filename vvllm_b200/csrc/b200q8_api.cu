@@ -1331,8 +1331,15 @@ int b200q8_linear_q8_sharded_p2p_ex(b200q8_comm* c, void* out, int out_dtype, co
         po.wait_counts = reinterpret_cast<const unsigned long long*>(c->flags.local);
         po.wait_n = G;
     }
-    if ((e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream)) != cudaSuccess)
-        return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");
+    // The shard runs on the kernel the local dispatch picks for it (b200q8_linear_q8, M <= 16):
+    // the streaming GEMV for a few tokens on a few MB of weights, else the int8 tensor-core GEMV.
+    const bool simt = M <= (size_t)gemv_max_tokens() && rows * K <= kSimtMaxWeightBytes &&
+                      gemv_stream_supports(a, d.max_smem);
+    if (simt)
+        e = launch_q8_gemv(a, d.num_sms, d.max_smem, (cudaStream_t)stream);
+    else
+        e = launch_q8_gemv_i8(a, d.num_sms, scratch, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "linear_q8_sharded_p2p: GEMV launch");
     // Behind the GEMV: publish this call once its grid has completed, and -- unless the wait is
     // deferred to the next gathered call or b200q8_comm_wait -- wait for every rank's part.
     const bool defer = (flags & B200Q8_P2P_DEFER_WAIT) != 0;

@@ -53,7 +53,7 @@ struct LinearArgs {
     size_t M = 0, N = 0, K = 0;
     int in_dtype = kF32, out_dtype = kF32;
     bool pdl = false;               // launch with programmatic stream serialization
-    const P2POut* p2p = nullptr;    // int8 digit GEMV only: gather into peers' outputs
+    const P2POut* p2p = nullptr;    // int8 digit GEMV and streaming GEMV (M <= 4): gather into peers' outputs
     // int8 digit GEMV only: greedy argmax of each token's outputs into amax_out[M] (keys and
     // counter are scratch that starts at zero and is left at zero).  out may then be null.
     unsigned long long* amax_keys = nullptr;
@@ -78,6 +78,9 @@ struct LinearArgs {
 // ranks; with `wait`, a bounded wait (timeout_ns) until every wait_counts[j], j < n, holds as
 // many whole calls as wait_counts[rank] (bit 1 of the error word on expiry).
 cudaError_t launch_p2p_sync(const P2POut& po, bool publish, bool wait, cudaStream_t stream);
+// Device address of that error word on the current device (looked up once per device), for the
+// other kernels a gathered call may run (the streaming GEMV); null if the lookup failed.
+int* p2p_error_word();
 
 // Streaming SIMT GEMV, M <= gemv_max_tokens().  Also takes any M/K through a
 // generic (slow, correct) kernel when the fast one cannot (alignment, K % 16).

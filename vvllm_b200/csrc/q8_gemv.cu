@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "p2p.cuh"
 #include "prologue.cuh"
 
 namespace b200q8 {
@@ -63,7 +64,34 @@ struct GemvParams {
     void* om[kMaxGroup];
     int Nm[kMaxGroup];
     int gofs[kMaxGroup + 1];
+    // Column-sharded gather (b200q8_linear_q8_sharded_p2p, one matrix): with ndst > 0 the output
+    // of row `row` for token t goes to dsts[d][t * ldo + ocol0 + row] on each of the ndst ranks
+    // instead of om[0]; with wait_counts set, every rank's part of the previous gathered call (x)
+    // must have landed before x is read (p2p.cuh), else bit 1 of *err.
+    int ndst, ocol0;
+    void* dsts[kMaxRanks];
+    const unsigned long long* wait_counts;
+    int wait_n, wait_rank;
+    unsigned long long wait_ns;
+    int* err;
 };
+
+// out = acc * scale (+ bias) (+ res), into the projection's own output, or -- gathered -- into
+// every rank's copy of the full output.
+template <typename OT>
+__device__ __forceinline__ void store_result(const GemvParams& p, int mi, int t, int row, const OT* res, float acc)
+{
+    if (p.ndst == 0) {
+        const long long o = (long long)t * p.Nm[mi] + row;
+        epilogue_store<OT>(reinterpret_cast<OT*>(p.om[mi]) + o, res ? res + o : nullptr, acc, p.sm[mi][row], p.bm[mi],
+                           row);
+        return;
+    }
+    float v = __fmul_rn(acc, p.sm[mi][row]);
+    if (p.bm[mi]) v = __fadd_rn(v, p.bm[mi][row]);
+    const long long o = (long long)t * p.ldo + p.ocol0 + row;
+    for (int d = 0; d < p.ndst; d++) store_from_f32<OT>(reinterpret_cast<OT*>(p.dsts[d]) + o, v);
+}
 
 // The matrix row group g belongs to.  Only this index and the group's offset stay in registers
 // across the streaming loop; the matrix's pointers are read from the parameters where used.
@@ -199,17 +227,25 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
     const int num_groups = p.gofs[p.nmat];
 
     // The weights do not depend on the previous kernel in the stream, x does: pull this CTA's
-    // first row group (one contiguous range of rows_per_cta rows, 16-byte aligned on this path)
-    // into L2 while that kernel finishes, then wait.
-    if (threadIdx.x == 0 && (int)blockIdx.x < num_groups) {
-        const int mi = group_matrix(p, (int)blockIdx.x);
-        const int r0 = ((int)blockIdx.x - p.gofs[mi]) * rows_per_cta;
-        const int nr = min(rows_per_cta, p.Nm[mi] - r0);
-        const unsigned bytes = (unsigned)((long long)nr * p.K);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wm[mi] + (long long)r0 * p.K), "r"(bytes)
-                     : "memory");
+    // row groups (each one contiguous range of rows_per_cta rows, 16-byte aligned on this path;
+    // at most 48 MiB in all, inside L2) into L2 while that kernel -- or, for a gathered call,
+    // the peers -- finish, then wait.
+    if (threadIdx.x == 0) {
+        for (int g = blockIdx.x; g < num_groups; g += gridDim.x) {
+            const int mi = group_matrix(p, g);
+            const int r0 = (g - p.gofs[mi]) * rows_per_cta;
+            const int nr = min(rows_per_cta, p.Nm[mi] - r0);
+            const unsigned bytes = (unsigned)((long long)nr * p.K);
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wm[mi] + (long long)r0 * p.K),
+                         "r"(bytes)
+                         : "memory");
+        }
     }
     pdl_wait();
+    if (p.wait_counts) {  // x is the gathered output of the previous call: every rank's part landed
+        if (threadIdx.x == 0 && !wait_peers(p.wait_counts, p.wait_n, p.wait_rank, p.wait_ns)) atomicOr(p.err, 2);
+        __syncthreads();
+    }
     if (p.pro != kProNone)
         stage_x_pro<XT>(xs4, reinterpret_cast<const XT*>(p.x), p.ldx, p.M, p.K, p.pro, p.norm_w, p.eps);
     else
@@ -282,11 +318,7 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
 #pragma unroll
                 for (int r = 0; r < R; r++) {
                     const int row = row0 + r;
-                    if (lane == t * R + r && t < p.M && row < p.Nm[mi]) {
-                        const long long o = (long long)t * p.Nm[mi] + row;
-                        epilogue_store<OT>(reinterpret_cast<OT*>(p.om[mi]) + o, res ? res + o : nullptr, v[t][r],
-                                           p.sm[mi][row], p.bm[mi], row);
-                    }
+                    if (lane == t * R + r && t < p.M && row < p.Nm[mi]) store_result<OT>(p, mi, t, row, res, v[t][r]);
                 }
         } else {
             float* buf = red + ((iter & 1) * kWarps + warp) * (MT * R);
@@ -305,9 +337,7 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
                     const float* base = red + ((iter & 1) * kWarps + rw * KW) * (MT * R);
                     float s = 0.f;
                     for (int k = 0; k < KW; k++) s += base[k * (MT * R) + lane];
-                    const long long o = (long long)t * p.Nm[mi] + row;
-                    epilogue_store<OT>(reinterpret_cast<OT*>(p.om[mi]) + o, res ? res + o : nullptr, s,
-                                       p.sm[mi][row], p.bm[mi], row);
+                    store_result<OT>(p, mi, t, row, res, s);
                 }
             }
         }
@@ -471,6 +501,18 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
     p.bm[0] = p.bias;
     p.om[0] = p.out;
     p.Nm[0] = p.N;
+    if (a.p2p) {  // the gathered call: the streaming kernel only
+        if (!gemv_stream_supports(a, max_smem) || a.M > 4 || a.res) return cudaErrorNotSupported;
+        p.ndst = a.p2p->ndst;
+        for (int d = 0; d < a.p2p->ndst; d++) p.dsts[d] = a.p2p->dst[d];
+        p.ldo = a.p2p->ldo;
+        p.ocol0 = a.p2p->ocol0;
+        p.wait_counts = a.p2p->wait_counts;
+        p.wait_n = a.p2p->wait_n;
+        p.wait_rank = a.p2p->rank;
+        p.wait_ns = a.p2p->wait_timeout_ns ? a.p2p->wait_timeout_ns : 2000000000ull;
+        if (!(p.err = p2p_error_word())) return cudaErrorInvalidSymbol;
+    }
     const bool x16 = (a.in_dtype == kF16);
     const bool o16 = (a.out_dtype == kF16);
     if (gemv_stream_supports(a, max_smem)) {

@@ -96,6 +96,9 @@ struct DigParams {
     long long units;
     P2POut po;        // output placement: local only (ndst = 1) or every rank's copy
     int fused_exps;   // exponents computed in-kernel (few tokens) instead of by the prep kernel
+    // Stages beyond the ring whose weight boxes the producer asks L2 for at the start (0: none):
+    // while the digitizers wait for the previous gathered call, HBM keeps streaming.
+    int prefetch_stages;
     // Greedy argmax over each token's outputs (null: none): packed (value, index) keys, zero
     // between launches; the launch's last CTA turns them into indices and re-zeroes them.
     unsigned long long* amax_keys;  // [M]
@@ -454,6 +457,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (ok && it.next(t, k0, k1)) {
                 const int row0 = t * kTileRows;
                 for (int kb = k0; kb < k1; kb++) {
+                    if (issued == S && p.prefetch_stages > 0) {
+                        // the ring is full: the next stages' boxes into L2 before the first wait
+                        sk::SegIter pit(u_begin, u_end, p.kbpt);
+                        int n = 0, pt, pk0, pk1;
+                        while (n < S + p.prefetch_stages && pit.next(pt, pk0, pk1))
+                            for (int pk = pk0; pk < pk1 && n < S + p.prefetch_stages; pk++, n++)
+                                if (n >= S)
+#pragma unroll
+                                    for (int h = 0; h < C::kBoxes; h++)
+                                        tc::tma_prefetch_l2_2d(&tmW, pk * BK + h * 128, pt * kTileRows);
+                    }
                     if (issued >= S &&
                         !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
                         raise_error(abort);
@@ -939,6 +953,15 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     const unsigned long long* prep_wait = p.fused_exps ? nullptr : p.po.wait_counts;
     if (!p.fused_exps) p.po.wait_counts = nullptr;
     const int G = (int)pick_grid_i8(tiles, p.kbpt, (long long)a.N * (long long)a.K, num_sms);
+    // A gathered call whose input is the previous call's gathered output waits for the peers
+    // before its first digits: stream the CTA's next stages into L2 meanwhile (up to 96 MB in
+    // all, well inside L2).
+    p.prefetch_stages = 0;
+    if (a.p2p && a.p2p->wait_counts) {
+        const long long per_cta = (p.units + G - 1) / G;
+        const long long budget = (96ll << 20) / ((long long)G * C::kWBytes);
+        p.prefetch_stages = (int)std::max(0ll, std::min(per_cta - S, budget));
+    }
     // A prologue: the prep kernel writes the activations once, the GEMV reads them as plain x.
     const bool materialize = a.prologue != kProNone;
     if ((long long)sc.ws_floats < 2LL * G * NC * kTileRows || (long long)sc.counters < tiles ||
@@ -1010,6 +1033,21 @@ cudaError_t launch_q8_gemv_i8(const LinearArgs& a, int num_sms, const TcScratch&
                                    : launch_typed<__half, float>(a, num_sms, sc, stream);
     return a.out_dtype == kF16 ? launch_typed<float, __half>(a, num_sms, sc, stream)
                                : launch_typed<float, float>(a, num_sms, sc, stream);
+}
+
+int* p2p_error_word()
+{
+    static std::mutex mu;
+    static int* word[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!word[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_kernel_error_i8) != cudaSuccess) return nullptr;
+        word[dev] = static_cast<int*>(ptr);
+    }
+    return word[dev];
 }
 
 cudaError_t launch_p2p_sync(const P2POut& po, bool publish, bool wait, cudaStream_t stream)

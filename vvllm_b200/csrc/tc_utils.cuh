@@ -104,6 +104,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// L2 prefetch of one 2-D tile of a tensor map: the bytes move from HBM into L2 only (no copy into
+// shared memory, no multicast), so a later tile load of the same box hits L2.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Untiled bulk copy global -> this CTA's shared memory, completing on an mbarrier
 // (no multicast).  Both addresses 16-byte aligned, `bytes` a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
