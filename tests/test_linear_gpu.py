@@ -196,6 +196,8 @@ FP16_BAD = [
     (1, 384, 24576, 0),      # wider: prep kernel, folded by the epilogue warps alone
     (2, 256, 896, 100),
     (3, 320, 8192, -5),      # several tokens on long rows: prep kernel
+    (8, 256, 896, 7),        # five tokens or more: the prep kernel's digit tiles
+    (6, 300, 3584, -2),
 ]
 
 
@@ -238,6 +240,67 @@ def test_i8_prep_kernel_scratch_across_token_counts(cuda, oracle):
                 assert np.all(np.isnan(y[i]))
             else:
                 assert rowwise_normwise_err(y[i], ref[i]) <= TOL_F32, (M, i)
+
+
+def _exact_i8_f16(xh, q, s, b, res):
+    """The digit kernel's fp16-activation result, emulated bit for bit: the exact dot product of
+    the int8 row and the fp16 activations (float64 is exact here: every product is a multiple of
+    2^-24 below 2^34 of them, every partial sum below 2^53 of them), rounded once to fp32, then
+    * scale (+ bias) (+ res) in fp32 and rounded to the output type."""
+    acc = (xh.astype(np.float64) @ q.astype(np.float64).T).astype(np.float32)
+    y = acc * s[None, :]
+    if b is not None:
+        y = y + b[None, :]
+    if res is not None:
+        y = y + res
+    return y
+
+
+# (M, N, K, fp16 outputs): one to four tokens digitize in-kernel; from five tokens on (and for
+# several tokens on long rows of large weights) the prep kernel makes each stage's digit tile once
+EXACT_F16 = [
+    (1, 300, 896, True), (2, 257, 3584, False), (4, 130, 1536, True), (5, 300, 896, True),
+    (8, 256, 3584, True), (8, 129, 16 * 37, False), (16, 384, 1536, True), (33, 200, 896, False),
+    (42, 130, 4864, True), (2, 3000, 12288, True),
+]
+
+
+@pytest.mark.parametrize("M,N,K,out16", EXACT_F16)
+def test_i8_fp16_exact_rounding(cuda, oracle, M, N, K, out16):
+    """With fp16 activations the digit kernel's outputs are the correctly rounded dot products:
+    bit-identical to an exact emulation, on both the in-kernel digits and the prep kernel's
+    digit tiles (stage tails, zero digit rows past 6M, ragged N)."""
+    import vvllm_b200 as v
+
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 140 + M))
+    x = make_x(M, K, 141 + M)
+    b = make_bias(N, 142)
+    res = make_x(M, N, 143) if M % 2 else None
+    y, xe, re = run_gpu(cuda, x, q, s, b, res, in16=True, out16=out16, algo=v.ALGO_TC_I8)
+    want = _exact_i8_f16(xe, q, s, b, re)
+    if out16:
+        want = want.astype(np.float16).astype(np.float32)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), float(np.max(np.abs(y - want)))
+
+
+def test_i8_fp16_digit_tiles_across_token_counts(cuda, oracle):
+    """The prep kernel's digit tiles live in per-stream scratch: calls with different token
+    counts (and digit-tile widths) in a row, one with an Inf, must each be exact."""
+    import vvllm_b200 as v
+
+    N, K = 320, 3584
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 150))
+    for M, seed in ((16, 151), (5, 152), (42, 153), (8, 154), (6, 155), (16, 156)):
+        x = make_x(M, K, seed)
+        if M == 6:
+            x[3, 1000] = np.inf
+        y, xe, _ = run_gpu(cuda, x, q, s, None, None, in16=True, algo=v.ALGO_TC_I8)
+        want = _exact_i8_f16(xe, q, s, None, None)
+        for i in range(M):
+            if M == 6 and i == 3:
+                assert np.all(np.isnan(y[i]))
+            else:
+                assert np.array_equal(y[i].view(np.uint32), want[i].view(np.uint32)), (M, i)
 
 
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs

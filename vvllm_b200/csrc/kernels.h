@@ -69,6 +69,9 @@ struct LinearArgs {
     // int8 digit GEMV only: find the per-token exponents in the prep kernel even where the GEMV
     // would scan x itself (lets a deferred peer wait be paid in the prep kernel on any shape).
     bool force_prep = false;
+    // int8 digit GEMV only: never have the prep kernel write the activations' digit tiles to
+    // scratch (the GEMV then digitizes every stage itself); the allocation-free entry sets it.
+    bool no_digit_images = false;
 };
 
 // The kernel behind a gathered call's GEMV (one thread does the work; it lets its own dependents
@@ -130,6 +133,8 @@ bool gemv_i8_supports(const LinearArgs& a);
 // True when the GEMV computes the per-token exponents itself (one launch, x read only in-kernel,
 // so a deferred peer wait can happen inside it).
 bool gemv_i8_fused_exps(const LinearArgs& a);
+// True when the GEMV's prep kernel writes every K-stage's digit tile to scratch once per launch.
+bool gemv_i8_images(const LinearArgs& a);
 int gemv_i8_max_tokens();
 void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, size_t* counters, size_t* act_bytes,
                           size_t* exps);

@@ -103,6 +103,10 @@ struct DigParams {
     // HBM keeps streaming while the digitizers wait for the previous kernel (or the previous
     // gathered call), and CTAs that start on SMs the previous kernel left idle fetch early.
     int prefetch_stages;
+    // Digit tiles of every K-stage, made once per launch by the prep kernel ([kbpt][kDBytes], each
+    // the exact shared-memory image of the stage's B tile) and copied in by the producer beside
+    // the weights; null: the digitizer warps make each stage's tile themselves.
+    const unsigned char* dig_img;
     int early_trigger;  // dependents may launch right after set-up (else at the epilogue's end)
     int w_evict_first;  // weight tiles are loaded with an L2 evict-first policy
     // Greedy argmax over each token's outputs (null: none): packed (value, index) keys, zero
@@ -351,6 +355,74 @@ __device__ __forceinline__ void digits6(long long q, uint32_t (&d)[kDigits], int
     d[kDigits - 1] |= (uint32_t)((int)(q >> 35) & 0xFF) << (8 * byte);
 }
 
+// The six digit words of 4 consecutive activations (one byte per activation) at exponent e.
+__device__ __forceinline__ void digit_words(const float (&v)[4], int e, uint32_t (&d)[kDigits])
+{
+#pragma unroll
+    for (int i = 0; i < kDigits; i++) d[i] = 0;
+    if (e != INT_MIN) {  // beyond K the values are 0: zero digits
+#pragma unroll
+        for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[i], e)), d, i);
+    }
+}
+
+// Stores token m's digit words for K offset kk (a multiple of 4, within the stage) into a stage's
+// B tile: digit i of token m is row 6m + i; boxes of [rows x 128 B], 128-byte swizzle.
+template <int kDBoxBytes>
+__device__ __forceinline__ void put_digit_words(unsigned char* tile, int m, int kk, const uint32_t (&d)[kDigits])
+{
+    const int h = kk >> 7, c = (kk & 127) >> 4, byte = kk & 15;
+#pragma unroll
+    for (int i = 0; i < kDigits; i++) {
+        const int r = m * kDigits + i;
+        *reinterpret_cast<uint32_t*>(tile + h * kDBoxBytes + r * 128 + ((c ^ (r & 7)) << 4) + byte) = d[i];
+    }
+}
+
+// Prep kernel of a launch whose GEMV copies its digit tiles in (fp16 activations, no prologue, no
+// gather; gemv_i8_images): grid = the kbpt K-stages, 256 threads.  CTA kb writes the exact
+// shared-memory image of stage kb's B tile -- every token's six digit rows at the fixed fp16
+// exponent, the same bytes the digitizer warps would write, and zero rows up to NC -- and
+// part[m * kbpt + kb] = -1 if token m's values in the stage hold an Inf/NaN, else 0 (folded by
+// the GEMV's epilogue warps like the scan words).  The digits are made once per launch instead of
+// once per tile and stage: with several tokens the digitizer warps were the GEMV's limit.
+template <int NC, int BK>
+__global__ void __launch_bounds__(kSqThreads) digit_tiles_kernel(const __half* __restrict__ x, int M, int K,
+                                                               int* __restrict__ part,
+                                                               unsigned char* __restrict__ img)
+{
+    pdl_launch_dependents();  // the GEMV may start streaming weights right away
+    pdl_wait();               // x is written by the previous kernel
+    constexpr int kIpt = BK / 4;  // items (4 consecutive k of one token) per token and stage
+    constexpr int kDBoxBytes = NC * 128;
+    __shared__ int bad[kMaxTokens];
+    const int kb = blockIdx.x, tid = threadIdx.x;
+    unsigned char* tile = img + (size_t)kb * (NC * BK);
+    for (int m = tid; m < M; m += kSqThreads) bad[m] = 0;
+    __syncthreads();
+    for (int item = tid; item < M * kIpt; item += kSqThreads) {
+        const int m = item / kIpt, kk = (item - m * kIpt) * 4, k = kb * BK + kk;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (k < K) load4<__half>(x + (size_t)m * K + k, v);
+        int nf = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) nf |= (fabsf(v[i]) <= FLT_MAX) ? 0 : 1;  // NaN and Inf fail
+        if (nf) atomicOr(&bad[m], 1);
+        uint32_t d[kDigits];
+        digit_words(v, kF16Exp, d);
+        put_digit_words<kDBoxBytes>(tile, m, kk, d);
+    }
+    // digit rows 6M .. NC-1: zero (16-byte chunks; all-zero rows need no swizzle)
+    constexpr int kChunks = BK / 16;  // per row
+    const int zr = kDigits * M;
+    for (int i = tid; i < (NC - zr) * kChunks; i += kSqThreads) {
+        const int r = zr + i / kChunks, c16 = i % kChunks;
+        *reinterpret_cast<uint4*>(tile + (c16 >> 3) * kDBoxBytes + r * 128 + (c16 & 7) * 16) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    for (int m = tid; m < M; m += kSqThreads) part[(size_t)m * gridDim.x + kb] = bad[m] ? -1 : 0;
+}
+
 __device__ __forceinline__ float recombine(const long long (&dsum)[kDigits], int e)
 {
     if (e == INT_MIN) return __int_as_float(0x7fc00000);  // the token row holds Inf/NaN
@@ -437,9 +509,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_mbar_init();
     }
     if (threadIdx.x == 32) tc::prefetch_tensormap(&tmW);
-    // Digit rows past 6M stay zero for the whole kernel: clear every stage's B tile once.
-    for (int i = threadIdx.x; i < S * C::kDBytes / 16; i += kThreads)
-        reinterpret_cast<uint4*>(sD)[i] = make_uint4(0, 0, 0, 0);
+    // Digit rows past 6M stay zero for the whole kernel: clear every stage's B tile once (the
+    // prep kernel's digit tiles carry their zero rows).
+    if (!p.dig_img)
+        for (int i = threadIdx.x; i < S * C::kDBytes / 16; i += kThreads)
+            reinterpret_cast<uint4*>(sD)[i] = make_uint4(0, 0, 0, 0);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
     __syncwarp();
     if (warp == 1) {
@@ -464,7 +538,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int t, k0, k1;
             sk::SegIter it(u_begin, u_end, p.kbpt);
-            const uint32_t sw_base = tc::smem_u32(sW);
+            const uint32_t sw_base = tc::smem_u32(sW), sd_base = tc::smem_u32(sD);
+            // With the prep kernel's digit tiles, each stage's full barrier also counts its digit
+            // tile's bytes.  The first S stages' weights are requested at once; their digit tiles
+            // (written by the prep kernel) only after griddepcontrol.wait, and every later stage
+            // requests both together.
+            const uint32_t stage_tx = C::kWBytes + (p.dig_img ? C::kDBytes : 0);
+            bool img_ready = false;
+            auto load_digits = [&](int q, int slot) {  // unit u_begin + q into ring slot `slot`
+                const long long u = u_begin + q;
+                const int kb = (int)(u - (u / p.kbpt) * p.kbpt);
+                tc::bulk_load(sd_base + slot * C::kDBytes, p.dig_img + (size_t)kb * C::kDBytes, C::kDBytes,
+                              full0 + 8u * slot);
+            };
+            auto catch_up = [&]() {  // digit tiles of the stages issued before the wait
+                pdl_wait();
+                for (int q = 0; q < issued; q++) load_digits(q, q);
+                img_ready = true;
+            };
             while (ok && it.next(t, k0, k1)) {
                 const int row0 = t * kTileRows;
                 for (int kb = k0; kb < k1; kb++) {
@@ -481,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 tc::tma_prefetch_l2_2d(&tmW, pk * BK + h * 128, pt * kTileRows);
                         }
                     }
+                    if (p.dig_img && issued == S) catch_up();
                     if (issued >= S &&
                         !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
                         raise_error(abort);
@@ -488,15 +580,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = full0 + 8u * st.idx;
-                    tc::mbar_arrive_expect_tx(fb, C::kWBytes);
+                    tc::mbar_arrive_expect_tx(fb, stage_tx);
 #pragma unroll
                     for (int h = 0; h < C::kBoxes; h++)
                         tc::tma_load_2d_hint(sw_base + st.idx * C::kWBytes + h * (kTileRows * 128), &tmW,
                                              kb * BK + h * 128, row0, fb, wpol);
+                    if (img_ready) load_digits(issued, st.idx);
                     issued++;
                     st.next(S);
                 }
             }
+            if (p.dig_img && !img_ready) catch_up();  // fewer stages than the ring holds
             if (*abort) {
                 const int zero = 0;
                 sk::Ring d;
@@ -525,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t d_tmem = tmem + ab * C::kDCols;
                 for (int kb = k0; kb < k1; kb++) {
                     if (!tc::mbar_wait(full0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs) ||
-                        !tc::mbar_wait(dfull0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs)) {
+                        (!p.dig_img && !tc::mbar_wait(dfull0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs))) {
                         raise_error(abort);
                         ok = false;
                         break;
@@ -575,7 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int* exps = s_exps;
         sk::Ring st;
         int g = 0, t, k0, k1;
-        sk::SegIter it(u_begin, u_end, p.kbpt);
+        // with the prep kernel's digit tiles the producer copies them in: nothing to do here
+        sk::SegIter it(u_begin, p.dig_img ? u_begin : u_end, p.kbpt);
         bool ok = true;
         const XT* xg = reinterpret_cast<const XT*>(p.x);
         // Thread -> items of 4 consecutive k of one token (BK/4 items per token per stage), at most
@@ -610,19 +705,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (item >= nitems) break;
                     const int m = item / (BK / 4);
                     const int kk = (item - m * (BK / 4)) * 4;  // 0..BK-4
-                    const int e = sizeof(XT) == 2 ? kF16Exp : exps[m];
-                    uint32_t d[kDigits] = {0, 0, 0, 0, 0, 0};
-                    if (e != INT_MIN) {  // beyond K the values are 0: zero digits
-#pragma unroll
-                        for (int i = 0; i < 4; i++) digits6(__float2ll_rn(ldexpf(v[j][i], e)), d, i);
-                    }
-                    const int h = kk >> 7, c = (kk & 127) >> 4, byte = kk & 15;
-#pragma unroll
-                    for (int i = 0; i < kDigits; i++) {
-                        const int r = m * kDigits + i;
-                        *reinterpret_cast<uint32_t*>(bst + h * C::kDBoxBytes + r * 128 + ((c ^ (r & 7)) << 4) + byte) =
-                            d[i];
-                    }
+                    uint32_t d[kDigits];
+                    digit_words(v[j], sizeof(XT) == 2 ? kF16Exp : exps[m], d);
+                    put_digit_words<C::kDBoxBytes>(bst, m, kk, d);
                 }
                 // generic-proxy writes -> visible to the tensor core's async-proxy reads
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -941,6 +1026,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
     const int ns = row_splits((long long)a.K);
     p.prep_part = sc.exps;
     p.prep_splits = ns;
+    p.dig_img = nullptr;
     p.fused_exps = gemv_i8_fused_exps(a) ? 1 : 0;
     p.amax_keys = a.amax_keys;
     p.amax_done = a.amax_done;
@@ -990,6 +1076,18 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& sc, cu
         sc.exps_count < a.M * (size_t)ns || (materialize && sc.act_bytes < a.M * a.K * sizeof(XT)))
         return cudaErrorMemoryAllocation;
     if (materialize) p.x = sc.act;
+    if constexpr (sizeof(XT) == 2) {
+        if (gemv_i8_images(a)) {  // the prep kernel makes every stage's digit tile once
+            if (sc.act_bytes < (size_t)p.kbpt * C::kDBytes || sc.exps_count < a.M * (size_t)p.kbpt)
+                return cudaErrorMemoryAllocation;
+            p.dig_img = sc.act;
+            p.prep_splits = p.kbpt;
+            e = launch_ex(digit_tiles_kernel<NC, BK>, dim3((unsigned)p.kbpt), dim3(kSqThreads), 0, stream, a.pdl,
+                          reinterpret_cast<const __half*>(a.x), (int)a.M, (int)a.K, sc.exps, sc.act);
+            if (e != cudaSuccess) return e;
+            return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, true, mw, p);
+        }
+    }
     if (p.fused_exps)  // one launch: the GEMV finds the exponents itself
         return launch_ex(kern, dim3((unsigned)G), dim3(kThreads), (size_t)C::kSmemBytes, stream, a.pdl, mw, p);
     e = launch_ex(exps_kernel<XT>, dim3((unsigned)a.M, (unsigned)ns), dim3(kSqThreads), 0, stream, a.pdl,
@@ -1025,6 +1123,15 @@ bool gemv_i8_fused_exps(const LinearArgs& a)
     return a.K <= kFusedExpMaxK || (a.N * a.K <= kInKernelScanMaxBytes && a.K <= kFusedExpMaxKSmall);
 }
 
+bool gemv_i8_images(const LinearArgs& a)
+{
+    // Several fp16 tokens (the prep kernel runs anyway): digit tiles made once per launch.  Not
+    // for fp32 (the digits need the scanned exponents first), a prologue (its prep kernel
+    // writes the activations), a gathered call, or the allocation-free entry.
+    return a.in_dtype == kF16 && a.prologue == kProNone && !a.p2p && !a.force_prep && !a.no_digit_images &&
+           !gemv_i8_fused_exps(a);
+}
+
 bool gemv_i8_supports(const LinearArgs& a)
 {
     const size_t xa = a.in_dtype == kF16 ? 8 : 16;  // 4-element vector loads of x
@@ -1043,6 +1150,12 @@ void gemv_i8_scratch_need(const LinearArgs& a, int num_sms, size_t* ws_floats, s
     *ws_floats = (size_t)(2 * G * NC * kTileRows);
     *counters = (size_t)tiles;
     // the prologue's activations, when the prep kernel writes them for the GEMV
+    const size_t kbpt = (a.K + BK - 1) / BK;
+    if (gemv_i8_images(a)) {  // the digit tiles [kbpt][NC x BK bytes] and one word per token and stage
+        *act_bytes = kbpt * (size_t)NC * (size_t)BK;
+        *exps = a.M * kbpt;
+        return;
+    }
     *act_bytes = (a.prologue != kProNone && !gemv_i8_fused_exps(a)) ? a.M * a.K * (a.in_dtype == kF16 ? 2 : 4) : 0;
     *exps = a.M * (size_t)row_splits((long long)a.K);  // the prep kernel's words
 }
@@ -1161,8 +1274,10 @@ int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t str
     }
     // The limits above keep every grid the launch can pick inside the array; check it anyway,
     // so a shape outside it is refused as such rather than reported as a failed allocation.
+    LinearArgs b = a;
+    b.no_digit_images = true;  // no scratch for digit tiles here
     size_t need_ws = 0, need_ctr = 0, need_act = 0, need_exps = 0;
-    gemv_i8_scratch_need(a, num_sms, &need_ws, &need_ctr, &need_act, &need_exps);
+    gemv_i8_scratch_need(b, num_sms, &need_ws, &need_ctr, &need_act, &need_exps);
     if (need_ws > kNoAllocPartialInts || need_ctr > (size_t)kNoAllocMaxTiles || need_exps > kNoAllocExps ||
         need_act > 0)
         return 5;
@@ -1177,7 +1292,7 @@ int launch_q8_gemv_i8_noalloc(const LinearArgs& a, int num_sms, cudaStream_t str
     sc.exps_count = kNoAllocExps;
     // the counters must start at zero: clear the ones this call uses (no allocation)
     if ((*err = cudaMemsetAsync(sc.counter_ptr, 0, tiles * sizeof(int), stream)) != cudaSuccess) return -1;
-    *err = launch_q8_gemv_i8(a, num_sms, sc, stream);
+    *err = launch_q8_gemv_i8(b, num_sms, sc, stream);
     return *err == cudaSuccess ? 0 : -1;
 }
 
