@@ -72,9 +72,19 @@ __device__ unsigned long long g_gemm_trace[1024][8];
         if (blockIdx.x < 1024)                                                                   \
             g_gemm_trace[blockIdx.x][slot] = (slot) == 0 ? tc::globaltimer_ns() : clock64() - (t0); \
     } while (0)
+// Per-CTA role counters of the profiling build: [cta][slot] = SM cycles a role spent waiting on
+// a barrier, or in its whole loop (slots listed with b200q8_trace_gemm_roles).
+__device__ unsigned long long g_gemm_role[1024][16];
+#define ROLE_TRACE(slot, v)                                                                        \
+    do {                                                                                           \
+        if (blockIdx.x < 1024) g_gemm_role[blockIdx.x][slot] = (unsigned long long)(v);           \
+    } while (0)
 #else
 #define GEMM_TRACE(slot, t0) \
     do {                     \
+    } while (0)
+#define ROLE_TRACE(slot, v) \
+    do {                    \
     } while (0)
 #endif
 
@@ -85,6 +95,20 @@ constexpr int kWarps = 14;
 constexpr int kThreads = kWarps * 32;
 constexpr int kFirstConv = 2, kFirstEpi = 10;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s: far above any legitimate wait
+
+// Bounded mbarrier wait; the profiling build adds the SM cycles it took to `acc`.
+__device__ __forceinline__ bool timed_wait(uint32_t bar, uint32_t parity, const volatile int* abort, long long& acc)
+{
+#ifdef B200Q8_TRACE
+    const long long t = clock64();
+    const bool r = tc::mbar_wait(bar, parity, abort, kWaitTimeoutNs);
+    acc += clock64() - t;
+    return r;
+#else
+    (void)acc;
+    return tc::mbar_wait(bar, parity, abort, kWaitTimeoutNs);
+#endif
+}
 
 struct SkParams {
     const float* scales;
@@ -98,6 +122,7 @@ struct SkParams {
     int tiles_n;        // weight-row tiles
     long long units;    // tiles * kbpt
     int tma_out;        // outputs leave by TMA store (16-byte aligned rows), else direct stores
+    int w_evict_first;  // weight tiles are read by one token tile only: L2 evict-first
 };
 
 template <int BN, int BK, int S, int SA>
@@ -117,6 +142,10 @@ struct SkCfg {
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                      : kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kChunk = BN < 32 ? BN : 32;    // accumulator columns per tcgen05.ld in the epilogue
+    // As many A stages in TMEM as shared-memory stages: they advance together, and one commit per
+    // stage frees both (the dequantizers wait on the stage's empty barrier).  A commit costs the
+    // issuing thread about as much as several MMAs.
+    static constexpr bool kOneCommit = (S == SA);
     static constexpr int kNumBars = 2 * S + 2 * SA + 2 * kAcc + 2;  // + accfull/accempty[kAcc], drain, fixup
     static constexpr int kOutBufBytes = kChunk * kTileRows * 4;  // one staged chunk (fp32 or fp16 outputs, fp32 partials)
     static constexpr int kSmemBytes = 1024 + S * (kW8Bytes + kXBytes) + 2 * kOutBufBytes + kNumBars * 8 + 16;
@@ -304,14 +333,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             int t, k0, k1;
             SegIter it(u_begin, u_end, p.kbpt);
             bool ok = true;
+            const uint64_t wpol = p.w_evict_first ? tc::l2_policy_evict_first() : tc::l2_policy_evict_normal();
+            long long w_empty = 0;
+            const long long t_role = clock64();
             while (ok && it.next(t, k0, k1)) {
                 const int row0 = (t % p.tiles_n) * kTileRows;
                 const int m0 = (t / p.tiles_n) * BN;
                 for (int kb = k0; kb < k1; kb++) {
                     const uint32_t fb = full0 + 8u * st.idx;
                     if (issued >= pre) {
-                        if (issued >= S &&
-                            !tc::mbar_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, kWaitTimeoutNs)) {
+                        if (issued >= S && !timed_wait(empty0 + 8u * st.idx, st.phase ^ 1u, abort, w_empty)) {
                             raise_error(abort);
                             ok = false;
                             break;
@@ -319,8 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc::mbar_arrive_expect_tx(fb, C::kW8Bytes + C::kXBytes);
 #pragma unroll
                         for (int h = 0; h < C::kWBoxes; h++)
-                            tc::tma_load_2d(sw_base + st.idx * C::kW8Bytes + h * C::kWBoxBytes, &tmW,
-                                            kb * BK + h * C::kWBoxW, row0, fb);
+                            tc::tma_load_2d_hint(sw_base + st.idx * C::kW8Bytes + h * C::kWBoxBytes, &tmW,
+                                                 kb * BK + h * C::kWBoxW, row0, fb, wpol);
                     }
                     const uint32_t xdst = sx_base + st.idx * C::kXBytes;
 #pragma unroll
@@ -330,6 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     st.next(S);
                 }
             }
+            ROLE_TRACE(11, w_empty);
+            ROLE_TRACE(12, clock64() - t_role);
             if (*abort) {
                 // drain: every copy this CTA issued lands before the CTA exits
                 const int zero = 0;
@@ -348,18 +381,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             SegIter it(u_begin, u_end, p.kbpt);
             bool ok = true;
             const uint64_t bdesc0 = tc::make_sw128_kmajor_desc(tc::smem_u32(sX));
+            long long w_full = 0, w_afull = 0, w_acc = 0, nstages = 0;
+            const long long t_role = clock64();
             while (ok && it.next(t, k0, k1)) {
                 const int ab = seg % C::kAcc, use = seg / C::kAcc;
-                if (use > 0 &&
-                    !tc::mbar_wait(accempty0 + 8u * ab, (uint32_t)((use - 1) & 1), abort, kWaitTimeoutNs)) {
+                if (use > 0 && !timed_wait(accempty0 + 8u * ab, (uint32_t)((use - 1) & 1), abort, w_acc)) {
                     raise_error(abort);
                     break;
                 }
                 tc::tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * C::kDCols;
-                for (int kb = k0; kb < k1; kb++) {
-                    if (!tc::mbar_wait(full0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs) ||
-                        !tc::mbar_wait(afull0 + 8u * sa.idx, sa.phase, abort, kWaitTimeoutNs)) {
+                for (int kb = k0; kb < k1; kb++, nstages++) {
+                    if (!timed_wait(full0 + 8u * st.idx, st.phase, abort, w_full) ||
+                        !timed_wait(afull0 + 8u * sa.idx, sa.phase, abort, w_afull)) {
                         raise_error(abort);
                         ok = false;
                         break;
@@ -375,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        b_stage + (uint64_t)(((j >> 2) * C::kXBoxBytes + (j & 3) * 32) >> 4), idesc,
                                        (kb != k0 || j != 0) ? 1u : 0u);
                     tc::mma_commit(empty0 + 8u * st.idx);
-                    tc::mma_commit(aempty0 + 8u * sa.idx);
+                    if constexpr (!C::kOneCommit) tc::mma_commit(aempty0 + 8u * sa.idx);
                     st.next(S);
                     sa.next(SA);
                 }
@@ -384,6 +418,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 GEMM_TRACE(4, trace_t0);
                 seg++;
             }
+            ROLE_TRACE(0, w_full);
+            ROLE_TRACE(1, w_afull);
+            ROLE_TRACE(2, w_acc);
+            ROLE_TRACE(3, clock64() - t_role);
+            ROLE_TRACE(4, nstages);
             if (*abort) {
                 const int zero = 0;
                 tc::mma_commit(drainbar);  // MMAs in flight finish before TMEM is freed
@@ -401,14 +440,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         int t, k0, k1;
         SegIter it(u_begin, u_end, p.kbpt);
         bool ok = true;
+        long long w_full = 0, w_aempty = 0;
+        const long long t_role = clock64();
         while (ok && it.next(t, k0, k1)) {
             for (int kb = k0; kb < k1; kb++, g++, st.next(S), sa.next(SA)) {
                 if ((g & 1) != group) continue;
-                ok = __all_sync(0xffffffffu, tc::mbar_wait(full0 + 8u * st.idx, st.phase, abort, kWaitTimeoutNs));
+                ok = __all_sync(0xffffffffu, timed_wait(full0 + 8u * st.idx, st.phase, abort, w_full));
                 if (!ok) break;
-                if (g >= SA) {
-                    ok = __all_sync(0xffffffffu,
-                                    tc::mbar_wait(aempty0 + 8u * sa.idx, sa.phase ^ 1u, abort, kWaitTimeoutNs));
+                if (g >= SA) {  // the MMAs that read this A stage last are done
+                    const uint32_t free_bar = C::kOneCommit ? empty0 + 8u * st.idx : aempty0 + 8u * sa.idx;
+                    ok = __all_sync(0xffffffffu, timed_wait(free_bar, sa.phase ^ 1u, abort, w_aempty));
                     if (!ok) break;
                 }
                 tc::tc_fence_after();
@@ -441,6 +482,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) tc::mbar_arrive(afull0 + 8u * sa.idx);
             }
         }
+        if (lane == 0 && q == 2) {  // warps 2 and 6: one of each group
+            ROLE_TRACE(5 + 3 * group, w_full);
+            ROLE_TRACE(6 + 3 * group, w_aempty);
+            ROLE_TRACE(7 + 3 * group, clock64() - t_role);
+        }
         if (!ok) raise_error(abort);
     } else {
         // ------------------------------------------------------------ epilogue
@@ -454,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int seg = 0, t, k0, k1;
         SegIter it(u_begin, u_end, p.kbpt);
         bool ok = true;
+        long long w_accfull = 0;
+        const long long t_role = clock64();
         // One chunk of outputs (tokens m .. m + CH - 1 of this thread's channel) goes
         // through a staging buffer in shared memory and leaves with one TMA store;
         // rows and columns beyond the output's extent are clipped by the store.
@@ -521,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float bias = (nv && has_bias) ? p.bias[n] : 0.0f;
             const OT* rrow = (p.res && nv) ? reinterpret_cast<const OT*>(p.res) + (size_t)m0 * p.N + n : nullptr;
             // one verdict for all four epilogue warps: named barrier 1 follows
-            ok = tc::bar_all<1, 128>(tc::mbar_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, kWaitTimeoutNs));
+            ok = tc::bar_all<1, 128>(timed_wait(accfull0 + 8u * ab, (uint32_t)(use & 1), abort, w_accfull));
             if (!ok) break;
             if (etid == 0 && seg == 0) GEMM_TRACE(5, trace_t0);
             tc::tc_fence_after();
@@ -668,6 +716,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) raise_error(abort);
         if (etid == 0) tc::bulk_wait_all();  // outputs written before the grid completes
         if (etid == 0) GEMM_TRACE(6, trace_t0);
+        if (etid == 0) {
+            ROLE_TRACE(13, w_accfull);
+            ROLE_TRACE(14, clock64() - t_role);
+        }
     }
 
     // ---------------------------------------------------------------- teardown
@@ -806,6 +858,10 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
     const long long tiles = (long long)p.tiles_n * (long long)((a.M + BN - 1) / BN);
     p.units = tiles * p.kbpt;
     p.tma_out = tma_out ? 1 : 0;
+    // Weight tiles read by one token tile only (M <= BN) are streamed through L2 once.  (Keeping
+    // weight stages requested into L2 ahead of the ring measured slower at M = 64: 7B lm_head
+    // 146 -> 150-156 us for 8-32 stages ahead.)
+    p.w_evict_first = a.M <= (size_t)BN ? 1 : 0;
     const int G = (int)pick_grid(tiles, p.kbpt, BN, BK, num_sms);
     if ((long long)scratch.ws_floats < 2LL * G * BN * kTileRows || (long long)scratch.counters < tiles)
         return cudaErrorMemoryAllocation;
@@ -829,11 +885,14 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
 template <typename OT>
 cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream)
 {
+    // One A stage in TMEM per shared-memory stage (one commit per stage).  Measured on B200 against
+    // the earlier layouts with fewer A stages (16: 5/2, 32: 4/2, 64: 6/3, 128: 4/3 stages), 7B
+    // projections back to back: M = 64 lm_head 153.4 -> 142.7 us, M = 8-16 1-4 % faster, M = 32 equal.
     switch (pick_bn(a.M, a.N, num_sms)) {
-        case 16: return launch_cfg<16, 256, 5, 2, OT>(a, num_sms, scratch, stream);
-        case 32: return launch_cfg<32, 256, 4, 2, OT>(a, num_sms, scratch, stream);
-        case 64: return launch_cfg<64, 128, 6, 3, OT>(a, num_sms, scratch, stream);
-        case 128: return launch_cfg<128, 128, 4, 3, OT>(a, num_sms, scratch, stream);
+        case 16: return launch_cfg<16, 256, 3, 3, OT>(a, num_sms, scratch, stream);
+        case 32: return launch_cfg<32, 256, 3, 3, OT>(a, num_sms, scratch, stream);
+        case 64: return launch_cfg<64, 128, 6, 6, OT>(a, num_sms, scratch, stream);
+        case 128: return launch_cfg<128, 128, 4, 4, OT>(a, num_sms, scratch, stream);
         default: return launch_cfg<256, 64, 4, 4, OT>(a, num_sms, scratch, stream);
     }
 }
@@ -877,6 +936,23 @@ extern "C" __attribute__((visibility("default"))) int b200q8_trace_gemm(void* ds
     }
     if (bytes > sizeof(g_gemm_trace)) bytes = sizeof(g_gemm_trace);
     return cudaMemcpyFromSymbol(dst, g_gemm_trace, bytes) == cudaSuccess ? 0 : -2;
+}
+
+// Profiling build only: copies the per-CTA role counters of the last GEMM launches, [1024][16]
+// SM cycles: 0-2 the MMA thread's waits (stage loaded, A stage dequantized, accumulator free),
+// 3 its whole loop, 4 its stage count; 5-7 and 8-10 one warp of each dequantizer group (waits
+// for the stage, for the A stage to be free, whole loop); 11-12 the producer (wait for a free
+// stage, whole loop); 13-14 the epilogue (wait for an accumulator, whole loop).
+// dst null: clear them.
+extern "C" __attribute__((visibility("default"))) int b200q8_trace_gemm_roles(void* dst, size_t bytes)
+{
+    if (!dst) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemm_role) != cudaSuccess) return -2;
+        return cudaMemset(p, 0, sizeof(g_gemm_role)) == cudaSuccess ? 0 : -2;
+    }
+    if (bytes > sizeof(g_gemm_role)) bytes = sizeof(g_gemm_role);
+    return cudaMemcpyFromSymbol(dst, g_gemm_role, bytes) == cudaSuccess ? 0 : -2;
 }
 #endif
 

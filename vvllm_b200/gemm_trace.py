@@ -3,6 +3,7 @@
     python -m vvllm_b200.gemm_trace build              # profiling copy of the library -> vvllm_b200/_trace/
     python -m vvllm_b200.gemm_trace phases [KxN ...]   # per-CTA phase times of one launch after an L2 flush
     python -m vvllm_b200.gemm_trace sweep              # per-call time back to back, every tile width / grid
+    python -m vvllm_b200.gemm_trace roles KxN:M ...    # per-role wait / loop cycles per K-stage of one launch
 
 The profiling copy is the same sources built with -DB200Q8_TRACE: the GEMM then stamps each CTA's
 phases (%globaltimer at its start, SM cycles to each phase after it) into a device array that
@@ -98,6 +99,46 @@ def phases(shapes) -> None:
               flush=True)
 
 
+ROLE_SLOTS = ["mma_wait_stage", "mma_wait_a", "mma_wait_acc", "mma_loop", "mma_stages",
+              "deq0_wait_stage", "deq0_wait_a_free", "deq0_loop", "deq1_wait_stage", "deq1_wait_a_free", "deq1_loop",
+              "prod_wait_free", "prod_loop", "epi_wait_acc", "epi_loop"]
+
+
+def roles(cases) -> None:
+    """Median over the CTAs of one launch (after three warm-up calls) of each role's barrier
+    waits and whole loop, in SM cycles per K-stage the CTA's MMA thread issued."""
+    import numpy as np
+    import torch
+
+    v, L = _load()
+    L.b200q8_trace_gemm_roles.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    L.b200q8_trace_gemm_roles.restype = ctypes.c_int
+    dev = torch.device("cuda", 0)
+    for case in cases:
+        shape, _, m = case.partition(":")
+        K, N = (int(a) for a in shape.split("x"))
+        Mt = int(m or M)
+        q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+        s = torch.rand(N, device=dev) * 1e-3
+        x = torch.randn(Mt, K, device=dev).half()
+        out = torch.empty(Mt, N, device=dev, dtype=torch.float16)
+        for _ in range(3):
+            v.linear_q8(out, x, q, s)
+        torch.cuda.synchronize()
+        buf = np.zeros((1024, 16), dtype=np.uint64)
+        L.b200q8_trace_gemm_roles(None, 0)  # cleared: CTAs of earlier launches leave no counts
+        torch.cuda.synchronize()
+        v.linear_q8(out, x, q, s)
+        torch.cuda.synchronize()
+        L.b200q8_trace_gemm_roles(buf.ctypes.data, buf.nbytes)
+        live = buf[:, 3] > 0
+        st = np.maximum(buf[live, 4].astype(np.float64), 1.0)
+        per = {name: round(float(np.median(buf[live, i] / st)), 1) for i, name in enumerate(ROLE_SLOTS) if i != 4}
+        print(f"K={K} N={N} M={Mt}", json.dumps(dict(ctas=int(live.sum()), stages_median=float(np.median(st)),
+                                                   loop_us=round(float(np.median(buf[live, 3])) / SM_MHZ, 2),
+                                                   cycles_per_stage=per)), flush=True)
+
+
 def sweep() -> None:
     import torch
 
@@ -163,5 +204,8 @@ if __name__ == "__main__":
         phases([tuple(int(a) for a in s.split("x")) for s in sys.argv[2:]] or SHAPES + [(3584, 37888)])
     elif cmd == "sweep":
         sweep()
+    elif cmd == "roles":
+        roles(sys.argv[2:] or ["3584x152064:64", "3584x37888:64", "18944x3584:64", "896x896:512",
+                              "4864x896:512", "896x4864:512", "3584x37888:512"])
     else:
         print(__doc__)
