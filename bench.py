@@ -964,20 +964,29 @@ def main():
             for it in range(args.warmup):
                 tok_step(it)
             barrier()
+            g = torch.cuda.CUDAGraph()  # the steps as one graph, like the headline
+            with torch.cuda.graph(g, stream=stream):
+                for it in range(nsteps):
+                    tok_step(it)
+            g.replay()
+            barrier()
             c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             c0.record(stream)
-            for it in range(nsteps):
-                tok_step(it)
+            g.replay()
             c1.record(stream)
             barrier()
+            del g
             t_step = c0.elapsed_time(c1) / nsteps
             nb = sum(algo_bytes(N, K, M) for _, N, K in PROJ)
             gbs = nb / (t_step * 1e-3) / 1e9
             tokens[f"M{M}"] = {"value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
                                "us_per_step": round(t_step * 1e3, 2),
                                "TFLOP/s": round(sum(2.0 * M * N * K for _, N, K in PROJ) / (t_step * 1e-3) / 1e12, 1),
-                               "kernel": "q8_gemv_dig_kernel (int8 tensor cores)" if M <= 16
-                               else "q8_gemm_sk_kernel (fp16 tensor cores)"}
+                               "timing": "one CUDA-graph replay of the steps",
+                               # the library's automatic choice (b200q8.h, B200Q8_ALGO_AUTO)
+                               "kernels": {n: ("q8_gemv_dig_kernel (int8 tensor cores)"
+                                               if M <= 4 or (M <= 8 and N >= 16384)
+                                               else "q8_gemm_sk_kernel (fp16 tensor cores)") for n, N, _ in PROJ}}
             del xm, om
         cfg1 = config1_gemv(v, dev, args.warmup, max(20, args.steps // 4), hbm_peak)
         prefill = prefill_tflops(v, dev, stream, args.warmup, max(5, args.steps // 10), tc_peak)

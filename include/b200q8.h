@@ -97,8 +97,8 @@ B200Q8_API int b200q8_linear_q8_add(void* out, int out_dtype, const void* inp, i
                          b200q8_stream_t stream);
 
 /* Kernel choice for b200q8_linear_q8_ex. */
-#define B200Q8_ALGO_AUTO 0  /* M <= 4 on <= 48 MiB of weights: SIMT; M <= 16: TC_I8; larger M: TC for fp16,
-                               TC_I8 (42-token groups) for fp32 */
+#define B200Q8_ALGO_AUTO 0  /* M <= 4 on <= 48 MiB of weights: SIMT; else M <= 4, or M <= 8 with
+                               N >= 16384: TC_I8; larger M: TC for fp16, TC_I8 (42-token groups) for fp32 */
 #define B200Q8_ALGO_SIMT 1  /* streaming SIMT GEMV (any dtype, any K; groups of <= 4 tokens) */
 #define B200Q8_ALGO_TC 2    /* tcgen05 kind::f16 GEMM, weights dequantized into TMEM (fp16 activations) */
 #define B200Q8_ALGO_TC_I8 3 /* tcgen05 kind::i8 GEMV on raw int8 weights, activations as exact 6-digit int8

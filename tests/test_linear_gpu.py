@@ -303,6 +303,29 @@ def test_i8_fp16_digit_tiles_across_token_counts(cuda, oracle):
                 assert np.array_equal(y[i].view(np.uint32), want[i].view(np.uint32)), (M, i)
 
 
+# 33-64 tokens: 64-token tiles with two MMA-issuing threads taking alternate K-stages into two
+# accumulators; stream-K segments of one stage (second accumulator unused), odd and even lengths
+TWO_ISSUERS = [
+    (64, 19000, 896),   # 149 row tiles of 7 stages on 148 CTAs: split segments of every length
+    (48, 20000, 1152),  # 9 stages per tile
+    (36, 4000, 3584),   # 28 stages per tile, few tiles
+    (64, 512, 3584),    # 4 tiles: one-stage segments
+]
+
+
+@pytest.mark.parametrize("M,N,K", TWO_ISSUERS)
+def test_gemm_two_issuers(cuda, oracle, M, N, K):
+    import vvllm_b200 as v
+
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 160 + M))
+    x = make_x(M, K, 161)
+    b = make_bias(N, 162)
+    res = make_x(M, N, 163) if M % 2 else None
+    for out16 in (True, False):
+        y, xe, re = run_gpu(cuda, x, q, s, b, res, in16=True, out16=out16, algo=v.ALGO_TC)
+        assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, re)) <= TOL_F16, out16
+
+
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs
 
 

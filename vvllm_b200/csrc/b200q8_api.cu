@@ -247,8 +247,13 @@ int linear_impl(void* out, int out_dtype, const void* inp, int in_dtype, const i
                     "linear_q8: int8 tensor-core path needs K %% 16 == 0, K <= 131072 and a 16-byte aligned "
                     "weight pointer (K=%zu)", K);
     const bool small = M <= (size_t)gemv_max_tokens() && N * K <= kSimtMaxWeightBytes;
+    // Few fp16 tokens: the int8 digit GEMV, which streams the raw weights, up to 4 tokens, and up
+    // to 8 on wide projections; beyond that the digit tiles (6 rows per token) cost more than the
+    // fp16 GEMM's dequantization.  Measured on B200, 7B projections at M = 8 (digit GEMV vs GEMM):
+    // lm_head 96 vs 111 us, gate/up 32 vs 31 us, down 33 vs 24 us; at M = 12 the GEMM wins on all.
+    const bool i8_first = M <= 4 || (M <= 8 && N >= 16384);
     const bool use_i8 = algo == B200Q8_ALGO_TC_I8 ||
-                        (algo == B200Q8_ALGO_AUTO && i8_ok && !small && (M <= 16 || !tc_ok));
+                        (algo == B200Q8_ALGO_AUTO && i8_ok && !small && (i8_first || !tc_ok));
     const bool use_tc =
         !use_i8 && (algo == B200Q8_ALGO_TC || (algo == B200Q8_ALGO_AUTO && tc_ok && !small));
     // The SIMT streaming kernel applies a prologue while it stages x (one launch); so does the

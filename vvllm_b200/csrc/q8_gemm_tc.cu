@@ -24,7 +24,7 @@
 // piece sums all pieces in K order (its own straight from TMEM), applies the
 // epilogue and resets the counter.  No CTA ever waits on another.
 //
-// Warp roles (14 warps):
+// Warp roles (14 warps, 15 with a second MMA-issuing thread):
 //   0      TMA producer: int8 weight tile [128 x BK] as swizzled boxes of
 //          [128 rows x min(BK,128) B] (64- or 128-byte swizzle) and fp16
 //          activation tile [BN x BK] as 128-byte-swizzled [BN x 64] boxes into
@@ -42,7 +42,9 @@
 //          weight copy ever touches shared memory or HBM;
 //   10..13 epilogue: tcgen05.ld of the finished accumulator, then
 //          v = acc * scale[n] (+ bias[n]) (+ res[m, n]) stored as fp16/fp32,
-//          or the stream-K partial/fixup path.
+//          or the stream-K partial/fixup path;
+//   14     (two-issuer layouts) a second thread issuing the MMAs of every other
+//          stage into its own accumulator; the epilogue adds the two.
 // Every mbarrier wait is bounded (wall clock); a timeout sets a device error
 // word, drains in-flight copies and MMAs, frees TMEM and returns.  No TMA
 // multicast and no thread-block clusters are used.
@@ -91,9 +93,8 @@ __device__ unsigned long long g_gemm_role[1024][16];
 namespace {
 
 constexpr int kTileRows = 128;  // weight rows per tile (UMMA M)
-constexpr int kWarps = 14;
-constexpr int kThreads = kWarps * 32;
 constexpr int kFirstConv = 2, kFirstEpi = 10;
+constexpr int kSecondIssuer = 14;  // warp of the second MMA-issuing thread (two-issuer layouts)
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s: far above any legitimate wait
 
 // Bounded mbarrier wait; the profiling build adds the SM cycles it took to `acc`.
@@ -125,7 +126,7 @@ struct SkParams {
     int w_evict_first;  // weight tiles are read by one token tile only: L2 evict-first
 };
 
-template <int BN, int BK, int S, int SA>
+template <int BN, int BK, int S, int SA, int NI>
 struct SkCfg {
     static constexpr int kWBoxW = BK < 128 ? BK : 128;  // bytes per weight-box row
     static constexpr int kWBoxes = BK / kWBoxW;
@@ -136,8 +137,10 @@ struct SkCfg {
     static constexpr int kXBytes = kXBoxes * kXBoxBytes;
     static constexpr int kACols = BK / 2;               // TMEM columns of one A stage
     static constexpr int kDCols = (BN + 31) / 32 * 32;  // one accumulator, 32-column aligned
-    static constexpr int kAcc = (2 * kDCols + SA * kACols <= 512) ? 2 : 1;
-    static constexpr int kACol = kAcc * kDCols;
+    // NI issuing threads, each with its own accumulator per buffer (they take alternate K-stages;
+    // the epilogue adds the two)
+    static constexpr int kAcc = (2 * NI * kDCols + SA * kACols <= 512) ? 2 : 1;
+    static constexpr int kACol = kAcc * NI * kDCols;
     static constexpr int kColsNeeded = kACol + SA * kACols;
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                      : kColsNeeded <= 256 ? 256 : 512;
@@ -146,7 +149,9 @@ struct SkCfg {
     // stage frees both (the dequantizers wait on the stage's empty barrier).  A commit costs the
     // issuing thread about as much as several MMAs.
     static constexpr bool kOneCommit = (S == SA);
-    static constexpr int kNumBars = 2 * S + 2 * SA + 2 * kAcc + 2;  // + accfull/accempty[kAcc], drain, fixup
+    static constexpr int kNumBars = 2 * S + 2 * SA + 2 * kAcc + 3;  // + accfull/accempty[kAcc], drain x2, fixup
+    static constexpr int kWarps = 14 + (NI - 1);
+    static constexpr int kThreads = kWarps * 32;
     static constexpr int kOutBufBytes = kChunk * kTileRows * 4;  // one staged chunk (fp32 or fp16 outputs, fp32 partials)
     static constexpr int kSmemBytes = 1024 + S * (kW8Bytes + kXBytes) + 2 * kOutBufBytes + kNumBars * 8 + 16;
     static_assert(kColsNeeded <= 512, "TMEM overflow");
@@ -155,6 +160,7 @@ struct SkCfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
     static_assert(kXBoxBytes % 1024 == 0 && kW8Bytes % 1024 == 0, "stages stay 1024-byte aligned");
     static_assert(BN % kChunk == 0, "epilogue chunks tile the accumulator");
+    static_assert(NI == 1 || NI == 2, "one or two issuing threads");
 };
 
 // Byte offset of 16-byte chunk c of row r inside a weight box, under the box's
@@ -217,6 +223,23 @@ struct Ring {
 
 // CH accumulator columns of this thread's TMEM lane, starting at column `col`.
 template <int CH>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t col, float (&v)[CH]);
+
+// The same columns summed over the issuers' accumulators: `col`, and `col + second` when second
+// is non-zero (the second issuer's accumulator, its stages' partial sum).
+template <int CH>
+__device__ __forceinline__ void tmem_ld_acc(uint32_t col, int second, float (&v)[CH])
+{
+    tmem_ld_chunk<CH>(col, v);
+    if (second) {
+        float w[CH];
+        tmem_ld_chunk<CH>(col + (uint32_t)second, w);
+#pragma unroll
+        for (int i = 0; i < CH; i++) v[i] += w[i];
+    }
+}
+
+template <int CH>
 __device__ __forceinline__ void tmem_ld_chunk(uint32_t col, float (&v)[CH])
 {
     if constexpr (CH == 32) {
@@ -235,12 +258,12 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t col, float (&v)[CH])
     }
 }
 
-template <int BN, int BK, int S, int SA, typename OT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int BK, int S, int SA, int NI, typename OT>
+__global__ void __launch_bounds__(SkCfg<BN, BK, S, SA, NI>::kThreads, 1)
     q8_gemm_sk_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                       const __grid_constant__ CUtensorMap tmO, const SkParams p)
 {
-    using C = SkCfg<BN, BK, S, SA>;
+    using C = SkCfg<BN, BK, S, SA, NI>;
     constexpr int CH = C::kChunk;
     constexpr int kRedSlotBytes = kTileRows * CH * 4;  // one piece's CH-column chunk
     constexpr int kRedSlots = S * (C::kW8Bytes + C::kXBytes) / kRedSlotBytes;
@@ -259,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t full0 = bar0, empty0 = bar0 + 8u * S, afull0 = bar0 + 16u * S,
                    aempty0 = bar0 + 16u * S + 8u * SA, accfull0 = bar0 + 16u * S + 16u * SA,
                    accempty0 = accfull0 + 8u * C::kAcc, drainbar = accempty0 + 8u * C::kAcc,
-                   redbar = drainbar + 8u;
+                   redbar = drainbar + 8u, drainbar2 = redbar + 8u;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -282,11 +305,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mbar_init(aempty0 + 8u * s, 1);
         }
         for (int b = 0; b < C::kAcc; b++) {
-            tc::mbar_init(accfull0 + 8u * b, 1);
+            tc::mbar_init(accfull0 + 8u * b, NI);  // every issuer commits
             tc::mbar_init(accempty0 + 8u * b, 4);
         }
         tc::mbar_init(drainbar, 1);
         tc::mbar_init(redbar, 1);
+        tc::mbar_init(drainbar2, 1);
         *abort = 0;
         tc::fence_mbar_init();
         // Weights do not depend on the previous kernel: start streaming them now.
@@ -372,8 +396,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (q + S >= requested) tc::mbar_wait(full0 + 8u * d.idx, d.phase, &zero, kWaitTimeoutNs);
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || (NI == 2 && warp == kSecondIssuer)) {
+        // ------------------------------------------------------------ MMA issuers
+        // With two issuing threads, issuer i takes the stages kb - k0 = i, i + 2, ... of each
+        // segment into its own accumulator (the epilogue adds them): one thread alone issues a
+        // tcgen05.mma only every ~60-120 cycles whatever N, two keep the tensor pipe busier.
+        const int issuer = warp == 1 ? 0 : 1;
         if (lane == 0) {
             constexpr uint32_t idesc = tc::make_idesc_f16_f32(kTileRows, BN);
             Ring st, sa;
@@ -390,8 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc::tc_fence_after();
-                const uint32_t d_tmem = tmem + ab * C::kDCols;
-                for (int kb = k0; kb < k1; kb++, nstages++) {
+                const uint32_t d_tmem = tmem + (ab * NI + issuer) * C::kDCols;
+                for (int kb = k0; kb < k1; kb++, st.next(S), sa.next(SA)) {
+                    if ((kb - k0) % NI != issuer) continue;
+                    nstages++;
                     if (!timed_wait(full0 + 8u * st.idx, st.phase, abort, w_full) ||
                         !timed_wait(afull0 + 8u * sa.idx, sa.phase, abort, w_afull)) {
                         raise_error(abort);
@@ -399,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc::tc_fence_after();
-                    if (seg == 0 && kb == k0) GEMM_TRACE(3, trace_t0);
+                    if (issuer == 0 && seg == 0 && kb == k0) GEMM_TRACE(3, trace_t0);
                     const uint32_t a_base = tmem + C::kACol + sa.idx * C::kACols;
                     // descriptor start address advances in 16-byte units
                     const uint64_t b_stage = bdesc0 + (uint64_t)((st.idx * C::kXBytes) >> 4);
@@ -407,29 +437,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < BK / 16; j++)
                         tc::mma_f16_ts(d_tmem, a_base + j * 8,
                                        b_stage + (uint64_t)(((j >> 2) * C::kXBoxBytes + (j & 3) * 32) >> 4), idesc,
-                                       (kb != k0 || j != 0) ? 1u : 0u);
+                                       (kb != k0 + issuer || j != 0) ? 1u : 0u);
                     tc::mma_commit(empty0 + 8u * st.idx);
                     if constexpr (!C::kOneCommit) tc::mma_commit(aempty0 + 8u * sa.idx);
-                    st.next(S);
-                    sa.next(SA);
                 }
                 if (!ok) break;
+                // an issuer with no stage in this segment commits too (it arrives at once)
                 tc::mma_commit(accfull0 + 8u * ab);
-                GEMM_TRACE(4, trace_t0);
+                if (issuer == 0) GEMM_TRACE(4, trace_t0);
                 seg++;
             }
-            ROLE_TRACE(0, w_full);
-            ROLE_TRACE(1, w_afull);
-            ROLE_TRACE(2, w_acc);
-            ROLE_TRACE(3, clock64() - t_role);
-            ROLE_TRACE(4, nstages);
+            if (issuer == 0) {
+                ROLE_TRACE(0, w_full);
+                ROLE_TRACE(1, w_afull);
+                ROLE_TRACE(2, w_acc);
+                ROLE_TRACE(3, clock64() - t_role);
+                ROLE_TRACE(4, nstages);
+            }
             if (*abort) {
                 const int zero = 0;
-                tc::mma_commit(drainbar);  // MMAs in flight finish before TMEM is freed
-                tc::mbar_wait(drainbar, 0, &zero, kWaitTimeoutNs);
+                const uint32_t db = issuer == 0 ? drainbar : drainbar2;
+                tc::mma_commit(db);  // this thread's MMAs in flight finish before TMEM is freed
+                tc::mbar_wait(db, 0, &zero, kWaitTimeoutNs);
             }
         }
-    } else if (warp < kFirstEpi) {
+    } else if (warp >= kFirstConv && warp < kFirstEpi) {
         // ------------------------------------------------------------ dequantize into TMEM
         const int group = (warp - kFirstConv) >> 2;  // 0 or 1: alternate stages
         const int q = warp & 3;                       // TMEM lane quadrant this warp may access
@@ -573,7 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             if (etid == 0 && seg == 0) GEMM_TRACE(5, trace_t0);
             tc::tc_fence_after();
-            const uint32_t d_tmem = tmem + t_lane + ab * C::kDCols;
+            const uint32_t d_tmem = tmem + t_lane + ab * NI * C::kDCols;
+            // the second issuer's accumulator holds stages only if the segment has two or more
+            const bool two = NI == 2 && k1 - k0 >= 2;
             const long long tb = (long long)t * p.kbpt;
             const bool whole = (k0 == 0 && k1 == p.kbpt);
             const int j0 = whole ? cta : cta_of_unit(tb, p.units, G);
@@ -634,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float acc[CH];
                         if (mode < 2) {
                             __syncwarp();
-                            tmem_ld_chunk<CH>(d_tmem + c0, acc);
+                            tmem_ld_acc<CH>(d_tmem + c0, two ? C::kDCols : 0, acc);
                         } else {
                             // pieces in K order: those before this CTA's, its own (from TMEM), the rest
                             const float4* sp = mode == 2 ? stage + (size_t)((c - cb) * others) * (kRedSlotBytes / 16) + r
@@ -646,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if (k == before) {
                                     float own[CH];
                                     __syncwarp();
-                                    tmem_ld_chunk<CH>(d_tmem + c0, own);
+                                    tmem_ld_acc<CH>(d_tmem + c0, two ? C::kDCols : 0, own);
 #pragma unroll
                                     for (int i = 0; i < CH; i++) acc[i] = before > 0 ? acc[i] + own[i] : own[i];
                                 }
@@ -821,10 +855,10 @@ long long pick_grid(long long tiles, long long kbpt, int BN, int BK, int num_sms
     return dp_us <= sk_us ? tiles : sk;
 }
 
-template <int BN, int BK, int S, int SA, typename OT>
+template <int BN, int BK, int S, int SA, int NI, typename OT>
 cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratch, cudaStream_t stream)
 {
-    using C = SkCfg<BN, BK, S, SA>;
+    using C = SkCfg<BN, BK, S, SA, NI>;
     CUtensorMap mw, mx, mo;
     if (!make_maps(a, BN, BK, &mw, &mx)) return cudaErrorInvalidValue;
     const size_t ob = a.out_dtype == kF16 ? 2 : 4;
@@ -834,7 +868,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
     } else {
         mo = mx;  // unused by the kernel
     }
-    auto kern = q8_gemm_sk_kernel<BN, BK, S, SA, OT>;
+    auto kern = q8_gemm_sk_kernel<BN, BK, S, SA, NI, OT>;
     static thread_local bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -869,7 +903,7 @@ cudaError_t launch_cfg(const LinearArgs& a, int num_sms, const TcScratch& scratc
     p.counters = scratch.counter_ptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)G);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(C::kThreads);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -888,12 +922,16 @@ cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& scra
     // One A stage in TMEM per shared-memory stage (one commit per stage).  Measured on B200 against
     // the earlier layouts with fewer A stages (16: 5/2, 32: 4/2, 64: 6/3, 128: 4/3 stages), 7B
     // projections back to back: M = 64 lm_head 153.4 -> 142.7 us, M = 8-16 1-4 % faster, M = 32 equal.
+    // 64-token tiles take two MMA-issuing threads (alternate stages, single-buffered accumulators):
+    // M = 64 lm_head 142.9 -> 126.9 us, gate/up 39.5 -> 33.5, down 31.0 -> 28.9 (with double-buffered
+    // accumulators and 4 stages: 135.2, 38.4, 32.7).  For 16- and 32-token tiles a second issuer
+    // measured within +-4 %, mostly slower.
     switch (pick_bn(a.M, a.N, num_sms)) {
-        case 16: return launch_cfg<16, 256, 3, 3, OT>(a, num_sms, scratch, stream);
-        case 32: return launch_cfg<32, 256, 3, 3, OT>(a, num_sms, scratch, stream);
-        case 64: return launch_cfg<64, 128, 6, 6, OT>(a, num_sms, scratch, stream);
-        case 128: return launch_cfg<128, 128, 4, 4, OT>(a, num_sms, scratch, stream);
-        default: return launch_cfg<256, 64, 4, 4, OT>(a, num_sms, scratch, stream);
+        case 16: return launch_cfg<16, 256, 3, 3, 1, OT>(a, num_sms, scratch, stream);
+        case 32: return launch_cfg<32, 256, 3, 3, 1, OT>(a, num_sms, scratch, stream);
+        case 64: return launch_cfg<64, 128, 6, 6, 2, OT>(a, num_sms, scratch, stream);
+        case 128: return launch_cfg<128, 128, 4, 4, 1, OT>(a, num_sms, scratch, stream);
+        default: return launch_cfg<256, 64, 4, 4, 1, OT>(a, num_sms, scratch, stream);
     }
 }
 
