@@ -3,9 +3,10 @@
 Each rank owns rows [r*ceil(N/G), ...) of the weight (b200q8_shard_range) and must end with the
 full [M, N] output, gathered by NCCL (b200q8_linear_q8_sharded) or by the GEMV's own stores into
 every rank's buffer (b200q8_linear_q8_sharded_p2p).  The gathered outputs must equal, bit for
-bit, each shard computed on one GPU by the local dispatch (b200q8_linear_q8 on the shard's rows:
-the kernel the gathered call runs per shard, so the same sums in the same order), and the CPU
-oracle on a row sample within the fp16 tolerance.
+bit, each shard computed on one GPU by the kernel the gathered call runs per shard (up to 4
+tokens the local dispatch's choice, b200q8_linear_q8 on the shard's rows; more tokens the int8
+digit GEMV), so the same sums in the same order, and the CPU oracle on a row sample within the
+fp16 tolerance.
 """
 import os
 import socket
@@ -43,8 +44,10 @@ def _free_port() -> int:
 
 
 def _sharded_ref(v, torch, dev, q, s, x, N, world, odt):
-    """Every shard's rows computed on this GPU by the local dispatch, assembled into [M, N]."""
+    """Every shard's rows computed on this GPU by the kernel the gathered call runs for them,
+    assembled into [M, N]."""
     M = x.shape[0]
+    algo = v.ALGO_AUTO if M <= 4 else v.ALGO_TC_I8
     out = torch.empty((M, N), dtype=odt, device=dev)
     qd, sd = torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev)
     for r in range(world):
@@ -52,7 +55,7 @@ def _sharded_ref(v, torch, dev, q, s, x, N, world, odt):
         if rows == 0:
             continue
         part = torch.empty((M, rows), dtype=odt, device=dev)
-        v.linear_q8(part, x, qd[r0:r0 + rows], sd[r0:r0 + rows])
+        v.linear_q8_ex(part, x, qd[r0:r0 + rows], sd[r0:r0 + rows], algo=algo)
         out[:, r0:r0 + rows] = part
     return out
 
