@@ -343,10 +343,9 @@ B200Q8_API int b200q8_comm_sym_free(b200q8_comm* comm, void* local);
  * on up to 48 MiB of weights (as b200q8_linear_q8 would pick), else the int8 tensor-core
  * GEMV: each rank's kernel stores
  * its [M, rows] slice straight into columns [row0, row0 + rows) of `out` on
- * EVERY rank (peer stores over NVLink).  Each CTA of that kernel then makes its
- * stores visible system-wide and counts itself in; the last one adds the call
- * to this rank's completion count on each rank.  A one-thread kernel behind the
- * GEMV then acquires every rank's count
+ * EVERY rank (peer stores over NVLink).  A one-thread kernel behind it, once the
+ * GEMV has completed, makes those stores visible system-wide and adds the call
+ * to its completion count on each rank, then acquires every rank's count
  * (bounded: 2 s, then bit 1 of b200q8_kernel_error).  After a bounded wait gave
  * up in the int8 GEMV (the error word is set) nothing more is published until
  * b200q8_kernel_error clears it, so the peers' waits run out as well instead of

@@ -13,16 +13,14 @@ enum DType : int { kF32 = 0, kF16 = 1 };
 // output element is stored into `ndst` copies of the full [M, ldo] output
 // (the local one and each peer's, mapped over NVLink), at column ocol0 + row.
 //
-// Completion: with `done` set (b200q8_linear_q8_sharded_p2p), the GEMV publishes
-// itself: each CTA, once its stores are issued, makes them visible system-wide
-// (one fence by one thread) and counts itself in at *done; the grid's last CTA
-// adds 2^20 to counts[rank] on every rank and leaves *done at zero.  Without it,
-// the small kernel launched behind the GEMV (launch_p2p_sync) passes
-// griddepcontrol.wait once the GEMV grid has completed and publishes the same
-// way.  So counts[j] on a rank holds 2^20 per call of rank j whose outputs have
-// landed there.  Nothing is published after a launch that set the device error
-// word (a bounded wait gave up): its peers' waits run out too, instead of reading
-// invalid outputs.
+// Completion: the GEMV's CTAs store and retire; they do not wait for the NVLink
+// acknowledgements of their stores.  The small kernel launched behind the GEMV
+// (launch_p2p_sync) passes griddepcontrol.wait once the GEMV grid has completed,
+// then one thread makes its stores visible system-wide (one fence) and adds 2^20
+// to counts[rank] on every rank.  So counts[j] on a rank holds 2^20 per call of
+// rank j whose outputs have landed there.  Nothing is published after a launch
+// that set the device error word (a bounded wait gave up): its peers' waits run
+// out too, instead of reading invalid outputs.
 //
 // Waits are relative, so nothing about them is fixed at launch time and the calls
 // can be captured in a CUDA graph and replayed: after the previous kernel in the
@@ -43,7 +41,6 @@ struct P2POut {
     const unsigned long long* wait_counts = nullptr;
     int wait_n = 0;
     unsigned long long wait_timeout_ns = 0;  // limit of that wait (0: the default, 2 s)
-    unsigned int* done = nullptr;  // this rank's arrival counter, zero at rest: in-kernel publish
 };
 
 struct LinearArgs {

@@ -22,24 +22,6 @@ __device__ __forceinline__ void publish_share(unsigned long long* const* counts,
     }
 }
 
-// One thread per CTA, once the CTA's stores to publish are issued and ordered before it (a
-// barrier): one system-scope fence makes them visible everywhere, then the CTA counts itself in
-// at *done.  The grid's last CTA (of nctas) leaves *done at zero for the next launch and, unless
-// the device error word *err is set, publishes the call (publish_share).
-__device__ __forceinline__ void arrive_and_publish(unsigned int* done, unsigned int nctas,
-                                                   unsigned long long* const* counts, int ndst, int rank,
-                                                   const int* err)
-{
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    unsigned int prev;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(done) : "memory");
-    if (prev != nctas - 1) return;
-    asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(done) : "memory");
-    int e;
-    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(e) : "l"(err) : "memory");
-    if (e == 0) publish_share(counts, ndst, rank, 1ull << kCountShift);
-}
-
 // One thread: bounded wait (timeout_ns of %globaltimer) until every counts[j], j < n, holds as
 // many whole calls as counts[self], this rank's own count, which is complete for every earlier
 // call once the previous kernel in the stream has finished.  Relaxed system-scope polls, then

@@ -74,10 +74,6 @@ struct GemvParams {
     int wait_n, wait_rank;
     unsigned long long wait_ns;
     int* err;
-    // With done set, the call publishes itself (p2p.cuh, arrive_and_publish): counts[d] on each
-    // of the ndst ranks, this rank = wait_rank.
-    unsigned long long* counts[kMaxRanks];
-    unsigned int* done;
 };
 
 // out = acc * scale (+ bias) (+ res), into the projection's own output, or -- gathered -- into
@@ -346,10 +342,6 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvParams p)
             }
         }
     }
-    if (p.done) {  // the gathered call publishes itself (p2p.cuh)
-        __syncthreads();  // every thread's stores are issued
-        if (threadIdx.x == 0) arrive_and_publish(p.done, gridDim.x, p.counts, p.ndst, p.wait_rank, p.err);
-    }
 }
 
 // Generic path for shapes the streaming kernel does not take (K % 16 != 0 or
@@ -520,8 +512,6 @@ cudaError_t launch_q8_gemv(const LinearArgs& a, int num_sms, size_t max_smem, cu
         p.wait_rank = a.p2p->rank;
         p.wait_ns = a.p2p->wait_timeout_ns ? a.p2p->wait_timeout_ns : 2000000000ull;
         if (!(p.err = p2p_error_word())) return cudaErrorInvalidSymbol;
-        for (int d = 0; d < a.p2p->ndst; d++) p.counts[d] = a.p2p->counts[d];
-        p.done = a.p2p->done;
     }
     const bool x16 = (a.in_dtype == kF16);
     const bool o16 = (a.out_dtype == kF16);

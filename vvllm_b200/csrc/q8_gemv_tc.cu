@@ -884,10 +884,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("bar.sync 1, 128;" ::: "memory");
             if (etid < p.M && s_best[etid]) atomicMax(p.amax_keys + etid, s_best[etid]);
         }
-        if (p.po.done) {  // the gathered call publishes itself (p2p.cuh)
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // every epilogue warp's stores are issued
-            if (etid == 0) arrive_and_publish(p.po.done, gridDim.x, p.po.counts, p.po.ndst, p.po.rank, &g_kernel_error_i8);
-        }
         if (!p.early_trigger) pdl_launch_dependents();
     }
 
