@@ -956,7 +956,11 @@ long long pick_grid_i8(long long tiles, long long kbpt, long long weight_bytes, 
     const long long units = tiles * kbpt;
     const long long all = units < num_sms ? units : num_sms;
     auto est = [&](long long G) {
-        const double bw = std::min(6.5e12, (double)G * 7.5e10);  // B/s (measured: ~75 GB/s per SM)
+        // B/s: ~60 GB/s per CTA in the decode step (with the L2 burst and the next projection's
+        // CTAs on the idle SMs), up to HBM.  Measured on B200, the 7B down projection (28 row
+        // tiles) inside the decode step: 84 CTAs 119.7-120.0 us per step, 112 CTAs 117.7-117.8,
+        // 148 CTAs 118.7-119.0, 56 CTAs 123.5-123.6.
+        const double bw = std::min(6.5e12, (double)G * 6.0e10);
         const long long pieces = (G + tiles - 1) / tiles;
         const double fix = pieces > 1 ? 1.0e-6 * (1.0 + (double)((pieces - 1 + 3) / 4)) : 0.0;
         return (double)weight_bytes / bw + fix;
