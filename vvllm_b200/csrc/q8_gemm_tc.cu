@@ -54,6 +54,7 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -840,9 +841,10 @@ long long pick_grid(long long tiles, long long kbpt, int BN, int BK, int num_sms
 {
     const long long units = tiles * kbpt;
 #ifdef B200Q8_TRACE
-    if (const char* f = getenv("B200Q8_TRACE_GRID")) {  // profiling build: 1 = whole tiles, 2 = stream-K
-        if (atoi(f) == 1) return tiles;
+    if (const char* f = getenv("B200Q8_TRACE_GRID")) {  // profiling build: 1 = whole tiles, 2 = stream-K,
+        if (atoi(f) == 1) return tiles;                  // larger: that many CTAs (at most the SMs)
         if (atoi(f) == 2) return units < num_sms ? units : num_sms;
+        if (atoi(f) > 2) return std::min<long long>(std::min<long long>(units, num_sms), atoi(f));
     }
 #endif
     const long long sk = units < num_sms ? units : num_sms;
@@ -852,7 +854,12 @@ long long pick_grid(long long tiles, long long kbpt, int BN, int BK, int num_sms
     const double dp_us = (double)kbpt * unit_us;
     const double pieces = (double)sk / (double)tiles + 1.0;
     const double sk_us = (double)units / (double)sk * unit_us + 12.0 + pieces;
-    return dp_us <= sk_us ? tiles : sk;
+    if (dp_us <= sk_us) return tiles;
+    // Splitting: as many pieces per tile for every tile when that keeps >= 90 % of the SMs (each
+    // tile's pieces then end together).  Measured on B200, 7B down projection (28 tiles): 140 CTAs
+    // vs 148 -- M = 64 26.2 vs 28.5 us, M = 8 23.1 vs 23.4 us.
+    const long long aligned = tiles * (sk / tiles);
+    return (aligned > tiles && 10 * aligned >= 9 * sk) ? aligned : sk;
 }
 
 template <int BN, int BK, int S, int SA, int NI, typename OT>
