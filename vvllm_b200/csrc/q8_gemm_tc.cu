@@ -931,7 +931,8 @@ cudaError_t launch_typed(const LinearArgs& a, int num_sms, const TcScratch& scra
     // projections back to back: M = 64 lm_head 153.4 -> 142.7 us, M = 8-16 1-4 % faster, M = 32 equal.
     // 64-token tiles take two MMA-issuing threads (alternate stages, single-buffered accumulators):
     // M = 64 lm_head 142.9 -> 126.9 us, gate/up 39.5 -> 33.5, down 31.0 -> 28.9 (with double-buffered
-    // accumulators and 4 stages: 135.2, 38.4, 32.7).  For 16- and 32-token tiles a second issuer
+    // accumulators and 4 stages: 135.2, 38.4, 32.7; with 256-wide K-stages, three of them: 128.7,
+    // 36.3, 28.8).  For 16- and 32-token tiles a second issuer
     // measured within +-4 %, mostly slower, on the 7B projections and on the config-4 GEMMs at
     // M = 512 (set of four 54.5 vs 54.7 us).
     switch (pick_bn(a.M, a.N, num_sms)) {
