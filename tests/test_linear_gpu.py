@@ -326,6 +326,23 @@ def test_gemm_two_issuers(cuda, oracle, M, N, K):
         assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, re)) <= TOL_F16, out16
 
 
+# Few row tiles on a long K: the GEMM splits every tile into the same number of pieces (28 tiles
+# x 5 pieces = 140 CTAs) and the digit GEMV picks its own grid (28 x 4); both against the oracle.
+FEW_TILES = [(8, 3584, 9472, "tc"), (64, 3584, 4096, "tc"), (1, 3584, 9472, "tc_i8"), (2, 3584, 9472, "tc_i8")]
+
+
+@pytest.mark.parametrize("M,N,K,algo_name", FEW_TILES)
+def test_few_row_tiles_split_grids(cuda, oracle, M, N, K, algo_name):
+    import vvllm_b200 as v
+
+    algo = {"tc": v.ALGO_TC, "tc_i8": v.ALGO_TC_I8}[algo_name]
+    q, s = oracle.quantize_per_channel(make_weight(N, K, 170 + M))
+    x = make_x(M, K, 171)
+    b = make_bias(N, 172)
+    y, xe, _ = run_gpu(cuda, x, q, s, b, None, in16=True, out16=True, algo=algo)
+    assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, None)) <= TOL_F16
+
+
 PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs
 
 
