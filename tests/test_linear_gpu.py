@@ -137,7 +137,7 @@ def test_fp16_paths_explicit(cuda, oracle, name, M, N, K, algo_name, out16):
 I8_FP32_SHAPES = [
     # fp32 activations on the int8 tensor-core kernel: exact digits must hold the 1e-5 bar
     ("i8_m1", 1, 4864, 896), ("i8_m1_k4864", 1, 896, 4864), ("i8_m2", 2, 300, 576), ("i8_m4", 4, 1536, 576),
-    ("i8_m5", 5, 200, 1536), ("i8_m16", 16, 640, 896), ("i8_m33", 33, 256, 3584), ("i8_m64", 64, 130, 896),
+    ("i8_m5", 5, 200, 1536), ("i8_m8", 8, 384, 1536), ("i8_m16", 16, 640, 896), ("i8_m33", 33, 256, 3584), ("i8_m64", 64, 130, 896),
     ("i8_m100", 100, 128, 576), ("i8_k16", 3, 50, 16), ("i8_k18944", 1, 448, 18944),
 ]
 
@@ -261,7 +261,7 @@ def _exact_i8_f16(xh, q, s, b, res):
 EXACT_F16 = [
     (1, 300, 896, True), (2, 257, 3584, False), (4, 130, 1536, True), (5, 300, 896, True),
     (8, 256, 3584, True), (8, 129, 16 * 37, False), (16, 384, 1536, True), (33, 200, 896, False),
-    (42, 130, 4864, True), (2, 3000, 12288, True),
+    (42, 130, 4864, True), (2, 3000, 12288, True), (6, 300, 3584, True), (7, 131, 896, False),
 ]
 
 
