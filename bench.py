@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Workload (M = 1 decode): the Qwen2.5-7B-shaped int8
+Workload (benchmark config 5, M = 1 decode): the Qwen2.5-7B-shaped int8
 projections -- fused gate/up 3584 -> 37888, down 18944 -> 3584 and lm_head
 3584 -> 152064 -- with fp16 activations, fp32 accumulation and fp16 outputs.
 Weights are synthetic N(0, 0.02), quantized per row by absmax on the GPU;
@@ -21,7 +21,7 @@ the 126 MB L2 (inputs larger than L2).  Output: one JSON line on rank 0.
 Beside the headline, the line carries: a parity verdict (N = 1: the reference's
 own CPU linear_q8 on a row sample of every projection; N > 1: every rank's
 gathered outputs against the unsharded digit GEMV of each rank's rows, bit for
-bit); BASELINE configs 1-4 and config 5 at M = 8 and 64 (rank 0, N = 1); the
+bit); benchmark configs 1-4 and config 5 at M = 8 and 64 (rank 0, N = 1); the
 GPU quantize against the reference's single-threaded quantize_per_channel; and
 the reference's CPU linear_q8 on working sets larger than twice the host's LLC.
 """
@@ -361,7 +361,7 @@ def cpu_quantize(lib, min_bytes: int, budget_s: float):
             "sample": f"[{R}, {K}] fp32 ({4 * R * K / 1e6:.0f} MB in), {iters} pass(es) in {el:.1f} s"}
 
 
-PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N), M = 512
+PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # benchmark config 4 (K, N), M = 512
 
 
 def prefill_tflops(v, dev, stream, warmup: int, iters: int, tc_peak: float):
@@ -432,7 +432,7 @@ def prefill_tflops(v, dev, stream, warmup: int, iters: int, tc_peak: float):
 
 
 def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
-    """BASELINE configs 2 and 3 as whole decode stacks at M = 1, each step one CUDA-graph replay
+    """benchmark configs 2 and 3 as whole decode stacks at M = 1, each step one CUDA-graph replay
     of every projection of every layer in order (the library's ctypes host call costs more than
     the small projections take on the device):
       SmolLM-135M-shaped, fp32 activations: 30 x {q 576, k/v 576->192, o 576 (+residual),
@@ -524,7 +524,7 @@ def decode_stacks(v, dev, warmup: int, iters: int, hbm_peak: float):
 
 
 def config1_gemv(v, dev, warmup: int, iters: int, hbm_peak: float):
-    """one fp32 decode GEMV, x [1, 896] -> y [1, 4864] (4.4 MB of int8 weights).
+    """benchmark config 1: one fp32 decode GEMV, x [1, 896] -> y [1, 4864] (4.4 MB of int8 weights).
     One CUDA graph runs the call once on each of enough weight copies to exceed 2x L2, so every
     call streams its weights from HBM; per-call time = median replay time / copies."""
     import torch
@@ -599,7 +599,7 @@ def profile_case(args):
 
     name, _, m = args.profile_case.partition(":")
     M = int(m) if m else 1
-    if "x" in name:  # explicit N x K (e.g. "4864x896:512", a prefill GEMM of BASELINE config 4)
+    if "x" in name:  # explicit N x K (e.g. "4864x896:512", a prefill GEMM of benchmark config 4)
         N, K = (int(v) for v in name.split("x"))
     else:
         N, K = {n: (N, K) for n, N, K in PROJ}[name]
@@ -946,7 +946,7 @@ def main():
         e_ms = t.item()
     e2e_value = total_bytes / (e_ms / args.steps * 1e-3) / 1e9
 
-    # ---- BASELINE config 5 at M = 8 and 64 tokens, configs 1-4, and the GPU quantize (rank 0, N = 1) ----
+    # ---- benchmark config 5 at M = 8 and 64 tokens, configs 1-4, and the GPU quantize (rank 0, N = 1) ----
     prefill = stacks = cfg1 = quant = None
     tokens = {}
     if world == 1:

@@ -149,7 +149,7 @@ def linear_small(ref: Reference) -> dict:
     return data
 
 
-# Full-size configs (3, 5 shapes); seeds as documented in tests.
+# Full-size configs (benchmark configs 1, 3, 5 shapes); seeds as documented in tests.
 DIGEST_CASES = [
     # name, N, K, weight seed, x seed
     ("config1_4864x896", 4864, 896, 1000, 42),

@@ -343,7 +343,7 @@ def test_few_row_tiles_split_grids(cuda, oracle, M, N, K, algo_name):
     assert rowwise_normwise_err(y, oracle_ref(oracle, xe, q, s, b, None)) <= TOL_F16
 
 
-PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # BASELINE config 4 (K, N) pairs
+PREFILL = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # benchmark config 4 (K, N) pairs
 
 
 @pytest.mark.parametrize("K,N", PREFILL)
@@ -455,7 +455,7 @@ def test_empty_and_streams(cuda, oracle):
 
 
 LARGE = [
-    # name, N, K, M  -- BASELINE config 3 lm_head and config 5 (7B) shapes at full size
+    # name, N, K, M  -- benchmark config 3 lm_head and config 5 (7B) shapes at full size
     ("qwen05b_lm_head", 151936, 896, 1),
     ("q7b_gate_up", 37888, 3584, 1),
     ("q7b_down", 3584, 18944, 1),

@@ -33,7 +33,7 @@ def _noalloc(out, x, w, s, b, res, stream):
 
 CASES = [
     # M, N, K, fp16 activations, bias, residual
-    (1, 4864, 896, True, True, False),     # BASELINE config 1 shape, decode
+    (1, 4864, 896, True, True, False),     # benchmark config 1 shape, decode
     (1, 448, 18944, True, False, True),    # 7B down-proj shard: every tile split (stream-K fixup)
     (2, 1000, 3584, False, True, True),    # fp32 activations, two tokens
     (1, 152064, 896, True, False, False),  # Qwen-0.5B lm_head width

@@ -1,4 +1,4 @@
-"""Profiling of the prefill GEMM (q8_gemm_sk_kernel) at BASELINE config 4 (M = 512, fp16).
+"""Profiling of the prefill GEMM (q8_gemm_sk_kernel) at benchmark config 4 (M = 512, fp16).
 
     python -m vvllm_b200.gemm_trace build              # profiling copy of the library -> vvllm_b200/_trace/
     python -m vvllm_b200.gemm_trace phases [KxN ...]   # per-CTA phase times of one launch after an L2 flush
