@@ -111,6 +111,7 @@ TC_SHAPES = [
     ("tc_m40", 40, 130, 896), ("tc_m64", 64, 512, 3584), ("tc_m100", 100, 200, 1536),
     ("tc_m128", 128, 256, 896), ("tc_m200", 200, 129, 576), ("tc_m300", 300, 384, 896),
     ("tc_k_tail", 8, 256, 16 * 37), ("tc_n1", 5, 1, 896), ("tc_n127", 2, 127, 128),
+    ("tc_n448_k18944", 1, 448, 18944),  # few rows on a long K: the 7B down shard at 8 GPUs
 ]
 
 
