@@ -1,4 +1,4 @@
-"""Profiling of the prefill GEMM (q8_gemm_sk_kernel) at benchmark config 4 (M = 512, fp16).
+"""Profiling build of the library: the fp16 GEMM (q8_gemm_sk_kernel) at benchmark config 4 (M = 512) and beyond.
 
     python -m vvllm_b200.gemm_trace build              # profiling copy of the library -> vvllm_b200/_trace/
     python -m vvllm_b200.gemm_trace phases [KxN ...]   # per-CTA phase times of one launch after an L2 flush
@@ -9,7 +9,12 @@ The profiling copy is the same sources built with -DB200Q8_TRACE: the GEMM then 
 phases (%globaltimer at its start, SM cycles to each phase after it) into a device array that
 b200q8_trace_gemm reads back, and its tile width / grid choice can be forced with the environment
 variables B200Q8_TRACE_BN (16, 32, 64, 128, 256) and B200Q8_TRACE_GRID (1 = one CTA per tile,
-2 = stream-K over all SMs).  The product library has neither.
+2 = stream-K over all SMs, larger = that many CTAs).  Each GEMM CTA also counts the SM cycles its
+roles spend waiting on their barriers and in their loops (b200q8_trace_gemm_roles, the `roles`
+command).  The profiling build's int8 digit GEMV takes B200Q8_TRACE_PF_MB (L2 burst at the start,
+MB over the grid), B200Q8_TRACE_EARLY (0: dependents launch at the epilogue's end) and
+B200Q8_TRACE_EVICT (0: weights loaded with the default L2 policy).  The product library has none
+of these.
 """
 from __future__ import annotations
 
