@@ -436,8 +436,10 @@ cudaError_t dispatch_typed(const GemvParams& p0, int num_sms, cudaStream_t strea
     // K split: aim for >= 2 chunks per lane per slice, up to 8 slices.
     int KW = 1;
     while (KW < 8 && C / (KW * 2) >= 64) KW *= 2;
-    // Few rows: split K harder so enough warps stream concurrently.
-    while (KW < 8 && (long long)p.N * KW < 64LL * num_sms && C / (KW * 2) >= 16) KW *= 2;
+    // Few rows: split K harder so enough warps stream concurrently -- but not past 4 slices on
+    // rows of 4096 and longer (Qwen2.5-0.5B down, 896 x 4864: 8 slices 4.66 us, 4 slices 4.19 us).
+    while (KW < 8 && (long long)p.N * KW < 64LL * num_sms && C / (KW * 2) >= 16 && !(KW >= 4 && p.K >= 4096))
+        KW *= 2;
     bool small_n = (long long)p.N < 4LL * num_sms * (8 / KW);
     // Few rows on a long K (the 7B down projection's shard at 8 GPUs, 448 x 18944): one row per
     // CTA would stage all of x in every CTA; four rows per CTA (K split 4, two rows per warp)
