@@ -35,6 +35,7 @@ def first_max(row):
     (1, 49152, 576, False, False),    # SmolLM lm_head, fp32 activations
     (3, 20000, 896, True, False),     # several tokens
     (1, 300, 18944, True, True),      # long K: every tile split over many stream-K pieces
+    (8, 30000, 3584, True, True),     # eight fp16 tokens: digit tiles made by the prep kernel
 ])
 def test_argmax_matches_logits(cuda, oracle, M, N, K, in16, out16):
     import torch
